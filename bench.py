@@ -1,0 +1,488 @@
+"""Benchmark of the dense-op hot path on B200 (one process per GPU).
+
+Headline workload: the row-reduction configuration, X [65536, 4096] f32
+~N(0,1) (seed 1 + rank) per GPU.  One step runs, through the C ABI, every
+operation the configuration names: per-row sum, max, argmax, softmax,
+layer-norm statistics (moments) and a global sum over all ranks' rows (one
+8-byte NCCL all-reduce).  The metric is algorithmic HBM bytes per second
+summed over all ranks (weak scaling: each rank owns 65536 rows).  X is 1.07 GB
+per pass, larger than the 126 MB L2, so no flush is needed between passes.
+
+The JSON line also reports, per convolution / attention workload, TFLOP/s
+against the roofline (key "ops"), the dominant kernel's roofline, the CPU
+baseline (the oracle on the host's cores) and an end-to-end number through
+host buffers.
+
+``--impl reference`` times the reference's CPU path (the oracle port of its
+f64 algorithms, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 65536, 4096
+METRIC = "conv/attn TFLOP/s and reduce HBM GB/s at 1/2/4/8 B200 vs roofline"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "sm_max_mhz": d.get("sm_max_mhz", 1965.0), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS, "bf16_tflops_sustained": 1400.0,
+            "sm_max_mhz": 1965.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            bus = parts[1].lower()
+            if self.bus_id and not (bus.endswith(self.bus_id[-12:]) or self.bus_id.endswith(bus[-12:])):
+                continue
+            rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, val in zip(names, r[6:10]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------- distributed
+
+class Dist:
+    def __init__(self, gpus: int):
+        import torch
+
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != gpus and gpus != 1:
+            print(f"warning: --gpus {gpus} but WORLD_SIZE {self.world}", file=sys.stderr)
+        self.torch = torch
+        self.pg = None
+
+    def init(self):
+        torch = self.torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            from datetime import timedelta
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                                 device_id=torch.device("cuda", self.local))
+            self.pg = torch.distributed.group.WORLD
+
+    def barrier(self):
+        if self.world > 1:
+            self.torch.distributed.barrier()
+
+    def max(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
+        self.torch.distributed.all_reduce(t)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.torch.distributed.destroy_process_group()
+
+
+# -------------------------------------------------------- row workload
+
+def row_ops(api, x, dist, timers=None):
+    """One step of the row workload.  Returns the per-row results."""
+    from forma_b200.api import ReduceOp
+
+    out = {}
+
+    def run(name, fn):
+        if timers is not None:
+            timers[name][0].record()
+        out[name] = fn()
+        if timers is not None:
+            timers[name][1].record()
+
+    run("row_sum", lambda: api.reduce_f32(ReduceOp.Sum, x, [1]))
+    run("row_max", lambda: api.reduce_f32(ReduceOp.Max, x, [1]))
+    run("row_argmax", lambda: api.argmax(x, 1))
+    run("softmax", lambda: api.softmax(x, [1]))
+    run("moments", lambda: api.moments(x, [1]))
+    run("global_sum", lambda: api.global_sum(x, dist.pg))
+    return out
+
+
+def row_bytes(rows: int, cols: int) -> dict:
+    """Algorithmic HBM bytes per launch of each operation."""
+    n = rows * cols * 4
+    return {"row_sum": n + rows * 4, "row_max": n + rows * 4, "row_argmax": n + rows * 4, "softmax": 2 * n,
+            "moments": n + 2 * rows * 4, "global_sum": n + 8}
+
+
+def cpu_baseline_rows(sample_rows: int, repeats: int = 1) -> dict:
+    """The oracle (the reference's f64 algorithms) on the host's cores, on a
+    sample of the row workload.  Returns bytes/s with the sample described."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    threads = orc.threads()
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((sample_rows, COLS)).astype(np.float32)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        orc.row_reduce(x, 0, threads)
+        orc.row_reduce(x, 3, threads)
+        orc.argmax_rows(x, threads)
+        orc.row_stats(x, 1e-5, threads, which=("softmax",))
+        orc.row_stats(x, 1e-5, threads, which=("mean", "variance"))
+        orc.sum_f64(x, threads)
+    dt = (time.perf_counter() - t0) / repeats
+    b = sum(row_bytes(sample_rows, COLS).values())
+    return {"value": b / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_rows} rows x {COLS} f32 through sum, max, argmax, softmax, moments, global sum "
+                      f"(oracle, f64 arithmetic, {threads} threads), {dt:.2f} s per pass"}
+
+
+# ------------------------------------------------- conv / attention workloads
+
+def _flush_l2(buf):
+    buf.add_(1)  # 256 MB written between timed launches: larger than the 126 MB L2
+
+
+def time_op(torch, fn, iters, flush_buf, stream):
+    """Average device time of fn over `iters` launches, L2 flushed before each."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in evs:
+        _flush_l2(flush_buf)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / iters
+
+
+def run_ops(api, dev, dist, args, pk) -> dict:
+    """Per-workload TFLOP/s of the convolution and attention configurations
+    (weak scaling: every rank runs the full configuration)."""
+    import torch
+
+    from forma_b200.api import AttentionOptions, ConvOptions
+
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(dist.rank)
+    iters = max(3, min(args.steps, 10))
+    res = {}
+    fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # FMA lanes x 2 FLOP x max clock
+
+    def record(name, fn, flops, peak, peak_name, note=None):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        ms = dist.max(time_op(torch, fn, iters, flush, stream))
+        tf = flops / (ms / 1e3) / 1e12
+        res[name] = {"tflops": round(dist.sum(tf), 2), "ms": round(ms, 4), "flop_per_call": flops,
+                     "roofline_frac": round(tf / peak, 4), "peak_tflops": round(peak, 1), "peak": peak_name}
+        if note:
+            res[name]["note"] = note
+
+    # C1: conv2d fp32 NCHW [8,64,56,56] x [64,64,3,3], stride 1, pad 1 (bit-faithful f32 path)
+    x = torch.rand(8, 64, 56, 56, device=dev, generator=g) * 2 - 1
+    w = torch.randn(64, 64, 3, 3, device=dev, generator=g) * math.sqrt(2 / 576)
+    o = ConvOptions([1, 1], [1, 1], [1, 1], [1, 1])
+    record("conv_f32_c1", lambda: api.conv(x, w, o), 2 * 8 * 64 * 56 * 56 * 64 * 9, fp32_peak,
+           "fp32 FMA peak (148 SMs x 128 lanes x 2 x max clock)",
+           "separate f32 multiply and add (reference order), so half the FMA peak is this kernel's ceiling")
+    del x, w
+    # C3a/C3b: ResNet-50 stage convs, bf16 NHWC, batch 256, f32 output
+    for name, cin, k, pad in (("conv_bf16_3x3_c3a", 256, 3, 1), ("conv_bf16_1x1_c3b", 1024, 1, 0)):
+        xn = torch.randn(256, 14, 14, cin, device=dev, generator=g).bfloat16()
+        wn = (torch.randn(256, k, k, cin, device=dev, generator=g) * math.sqrt(2 / (cin * k * k))).bfloat16()
+        xv, wv = xn.permute(0, 3, 1, 2), wn.permute(0, 3, 1, 2)
+        out = torch.empty(256, 14, 14, 256, device=dev).permute(0, 3, 1, 2)  # NHWC f32 storage, NCHW view
+        oc = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
+        record(name, lambda: api.conv_low_f32_into(xv, wv, oc, out), 2 * 256 * 14 * 14 * 256 * cin * k * k,
+               pk["bf16_tflops"], "measured bf16 dense (burst)")
+        del xn, wn, out
+    return res
+
+
+# ------------------------------------------------------------------ main
+
+def run_forma(args) -> int:
+    import torch
+
+    dist = Dist(args.gpus)
+    dist.init()
+    from forma_b200 import api
+
+    dev = torch.device("cuda", dist.local)
+    pk = peaks()
+    g = torch.Generator(device=dev).manual_seed(1 + dist.rank)
+    x = torch.randn(ROWS, COLS, device=dev, generator=g, dtype=torch.float32)
+    bytes_per = row_bytes(ROWS, COLS)
+    step_bytes = sum(bytes_per.values())
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        row_ops(api, x, dist)
+    torch.cuda.synchronize(dev)
+
+    # device-resident timed region
+    timers = {k: [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.steps)]
+              for k in bytes_per}
+    per_kernel_ms = {k: 0.0 for k in bytes_per}
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        bus = None
+    launches0 = api.launch_count()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(bus if isinstance(bus, str) else None) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step_timers = {k: v[i] for k, v in timers.items()}
+            row_ops(api, x, dist, step_timers)
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    launches = api.launch_count() - launches0
+    local_ms = start.elapsed_time(stop)
+    for k, evs in timers.items():
+        per_kernel_ms[k] = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    total_ms = dist.max(local_ms)
+    value = dist.sum(step_bytes * args.steps) / (total_ms / 1e3) / 1e9
+
+    dom = max(per_kernel_ms, key=per_kernel_ms.get)
+    achieved = bytes_per[dom] / (per_kernel_ms[dom] / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / f"{dom}_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+
+    # end to end: pinned host input copied in, results read back, every step
+    host_x = torch.empty(ROWS, COLS, dtype=torch.float32, pin_memory=True)
+    host_x.copy_(x.cpu())
+    outs_host = {k: torch.empty(ROWS, dtype=torch.float32, pin_memory=True) for k in ("row_sum", "row_max", "mean", "var")}
+    arg_host = torch.empty(ROWS, dtype=torch.int32, pin_memory=True)
+    gs_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(2, min(args.steps, 5))
+
+    def e2e_step():
+        x_dev.copy_(host_x, non_blocking=True)
+        r = row_ops(api, x_dev, dist)
+        outs_host["row_sum"].copy_(r["row_sum"], non_blocking=True)
+        outs_host["row_max"].copy_(r["row_max"], non_blocking=True)
+        arg_host.copy_(r["row_argmax"], non_blocking=True)
+        outs_host["mean"].copy_(r["moments"].mean, non_blocking=True)
+        outs_host["var"].copy_(r["moments"].variance, non_blocking=True)
+        gs_host.copy_(r["global_sum"], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = dist.max(e0.elapsed_time(e1))
+    e2e_value = dist.sum(step_bytes * e2e_steps) / (e2e_ms / 1e3) / 1e9
+    h2d = ROWS * COLS * 4
+    d2h = ROWS * 4 * 5 + 4
+
+    ops = {}
+    if not args.no_ops:
+        ops = run_ops(api, dev, dist, args, pk)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_rows(args.cpu_rows)
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "row reductions: X [65536, 4096] f32 ~N(0,1) per GPU; per-row sum, max, argmax, "
+                                   "softmax, layer-norm moments; global sum over all ranks (one f64 all-reduce)",
+                       "rows_per_gpu": ROWS, "cols": COLS, "parallelism": f"rows sharded over {dist.world} GPU(s)",
+                       "l2": "inputs larger than L2 (1.07 GB per pass), no flush",
+                       "bytes_per_step_per_gpu": step_bytes},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                         "peak_source": pk["source"]},
+            "kernels_ms": {k: round(v, 4) for k, v in per_kernel_ms.items()},
+            "kernels_frac_of_hbm": {k: round(bytes_per[k] / (v / 1e3) / 1e9 / pk["hbm_gbs"], 4)
+                                    for k, v in per_kernel_ms.items()},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "ops": ops,
+        }
+        print(json.dumps(line), flush=True)
+    dist.close()
+    return 0
+
+
+def run_reference(args) -> int:
+    """The reference's CPU path (oracle port, all host threads), bounded sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    threads = orc.threads()
+    rows = args.cpu_rows
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((rows, COLS)).astype(np.float32)
+    b = sum(row_bytes(rows, COLS).values())
+
+    def step():
+        orc.row_reduce(x, 0, threads)
+        orc.row_reduce(x, 3, threads)
+        orc.argmax_rows(x, threads)
+        orc.row_stats(x, 1e-5, threads, which=("softmax",))
+        orc.row_stats(x, 1e-5, threads, which=("mean", "variance"))
+        orc.sum_f64(x, threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = b / dt / 1e9
+    sample = (f"{rows} of {ROWS} rows x {COLS} f32 per step through sum, max, argmax, softmax, moments, global sum "
+              f"(oracle port of the reference's f64 algorithms, {threads} threads)")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "row reductions: X [65536, 4096] f32 ~N(0,1); per-row sum, max, argmax, softmax, "
+                               "layer-norm moments; global sum", "rows_per_gpu": ROWS, "cols": COLS},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["forma", "reference"], default="forma")
+    ap.add_argument("--cpu-rows", type=int, default=2048)
+    ap.add_argument("--no-ops", action="store_true", help="skip the conv/attention workloads")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "forma":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_forma(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

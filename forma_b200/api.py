@@ -1,0 +1,402 @@
+"""Operator API of the B200 dense-op backend, mirroring Forma's tensor-core traits.
+
+Each function corresponds to one trait method of the reference and keeps its
+name, argument meaning, output shape and error behaviour:
+
+==========================  =====================================================
+this module                 reference (crates/tensor-core/src/...)
+==========================  =====================================================
+``conv``                    ``TensorConvBackend::conv`` (convolution.rs:125-132)
+``conv_low_f32``/``conv_low``  ``TensorLowConvBackend`` (low_convolution.rs:16-44)
+``attention``               ``TensorAttentionBackend::attention`` (attention.rs:49-58)
+``attention_low_f32``       ``TensorLowAttentionBackend`` (low_attention.rs:28-49)
+``reduce_f32``/``reduce_u32``/``mean_axes``  ``TensorReduceBackend`` (reduction.rs:20-41)
+``softmax`` ... ``layer_norm``  ``TensorStatsBackend`` (statistics.rs:100-129), and the
+                            ``*_low_f32`` methods of ``TensorLowStatsBackend`` for
+                            f16/bf16 inputs (low_statistics.rs:25-57)
+``argmax``                  new: ``Tensor::topk``'s ordering (host_tensor/similarity.rs:82)
+``global_sum``              ``reduce_f32(Sum, all axes)`` with rows sharded over ranks
+==========================  =====================================================
+
+Tensors are torch CUDA tensors used purely as device memory: any strided view
+(permuted, broadcast via ``expand``, offset) is passed through as a layout
+descriptor, like the reference's ``CudaTensor`` = storage + ``Layout``.  F16 and
+BF16 tensors are the reference's low storage (the same 16-bit patterns).
+Outputs are freshly allocated and contiguous, like ``CudaRuntime::zeros``.
+Errors raise :class:`TensorError` with the reference's error kind.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from enum import IntEnum
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import FbAttentionOptions, FbConvOptions, FbTensor
+
+_DTYPES = {torch.float32: _lib.F32, torch.int32: _lib.U32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+# u32 tensors are held as torch.int32 storage (same bits; torch has no uint32 arithmetic on CUDA).
+_TORCH = {_lib.F32: torch.float32, _lib.U32: torch.int32, _lib.F16: torch.float16, _lib.BF16: torch.bfloat16}
+
+
+class TensorError(RuntimeError):
+    """A non-zero status from the C ABI; ``kind`` is the reference's variant name."""
+
+    def __init__(self, status: int, detail: str):
+        self.status = status
+        self.kind = _lib.STATUS_NAMES.get(status, f"Status{status}")
+        super().__init__(f"{self.kind}: {detail}")
+
+
+class ReduceOp(IntEnum):
+    """tensor_core::ReduceOp (reduction.rs:6-13)."""
+
+    Sum = 0
+    Product = 1
+    Min = 2
+    Max = 3
+
+
+@dataclass
+class ConvOptions:
+    """tensor_core::ConvOptions (convolution.rs:7-26)."""
+
+    strides: list = field(default_factory=list)
+    dilations: list = field(default_factory=list)
+    padding_before: list = field(default_factory=list)
+    padding_after: list = field(default_factory=list)
+    groups: int = 1
+
+    @classmethod
+    def new(cls, spatial_rank: int) -> "ConvOptions":
+        return cls([1] * spatial_rank, [1] * spatial_rank, [0] * spatial_rank, [0] * spatial_rank, 1)
+
+
+@dataclass
+class AttentionOptions:
+    """tensor_core::AttentionOptions (attention.rs:3-13)."""
+
+    scale: Optional[float] = None
+    causal: Optional[int] = None
+
+
+@dataclass
+class Mask:
+    """tensor_core::AttentionMask: ``kind`` is "keep" (u32/int32 tensor) or "additive" (f32)."""
+
+    kind: str
+    tensor: torch.Tensor
+
+
+@dataclass
+class Moments:
+    mean: torch.Tensor
+    variance: torch.Tensor
+
+
+def lib() -> C.CDLL:
+    return _lib.load()
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise TensorError(status, lib().fb_last_error().decode(errors="replace"))
+
+
+def describe(t: torch.Tensor) -> FbTensor:
+    """Layout descriptor of a torch tensor view (storage + strides + offset, in elements)."""
+    if t.dtype not in _DTYPES:
+        raise TensorError(33, f"unsupported dtype {t.dtype}")
+    if t.dim() > _lib.MAX_RANK:
+        raise TensorError(32, f"rank {t.dim()} exceeds {_lib.MAX_RANK}")
+    if any(s < 0 for s in t.stride()):
+        raise TensorError(32, "negative strides require materialization")
+    d = FbTensor()
+    st = t.untyped_storage()
+    d.data = st.data_ptr() if st.nbytes() else None
+    d.storage_len = st.nbytes() // t.element_size()
+    d.dtype = _DTYPES[t.dtype]
+    d.rank = t.dim()
+    for i, (n, s) in enumerate(zip(t.shape, t.stride())):
+        d.dims[i] = n
+        d.strides[i] = s
+    d.offset = t.storage_offset()
+    return d
+
+
+def _stream(device: torch.device):
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _device(*ts: torch.Tensor) -> torch.device:
+    for t in ts:
+        if t is not None:
+            if t.device.type != "cuda":
+                raise TensorError(32, "tensors must be CUDA device memory (no CPU fallback)")
+            return t.device
+    raise TensorError(32, "no tensor")
+
+
+def _conv_options(o: ConvOptions):
+    keep = [_lib.u64_array(o.strides), _lib.u64_array(o.dilations), _lib.u64_array(o.padding_before),
+            _lib.u64_array(o.padding_after)]
+    opts = FbConvOptions(
+        C.cast(keep[0], _lib.U64P), len(o.strides),
+        C.cast(keep[1], _lib.U64P), len(o.dilations),
+        C.cast(keep[2], _lib.U64P), len(o.padding_before),
+        C.cast(keep[3], _lib.U64P), len(o.padding_after),
+        o.groups,
+    )
+    return opts, keep
+
+
+def _attn_options(o: AttentionOptions) -> FbAttentionOptions:
+    return FbAttentionOptions(
+        1 if o.scale is not None else 0,
+        float(o.scale) if o.scale is not None else 0.0,
+        1 if o.causal is not None else 0,
+        int(o.causal) if o.causal is not None else 0,
+    )
+
+
+# ----------------------------------------------------------------- plans
+
+def conv_plan(input_shape: Sequence[int], weight_shape: Sequence[int], options: ConvOptions) -> list:
+    """ConvPlan::new output dims (host only)."""
+    opts, _keep = _conv_options(options)
+    out = (C.c_uint64 * _lib.MAX_RANK)()
+    rank = C.c_uint32()
+    _check(lib().fb_conv_plan(_lib.u64_array(input_shape), len(input_shape), _lib.u64_array(weight_shape),
+                              len(weight_shape), C.byref(opts), out, C.byref(rank)))
+    return [out[i] for i in range(rank.value)]
+
+
+def attention_plan(q: Sequence[int], k: Sequence[int], v: Sequence[int], mask: Optional[Sequence[int]],
+                   options: AttentionOptions) -> list:
+    """AttentionPlan::new output dims (host only)."""
+    out = (C.c_uint64 * _lib.MAX_RANK)()
+    rank = C.c_uint32()
+    m = _lib.u64_array(mask) if mask is not None else None
+    _check(lib().fb_attention_plan(_lib.u64_array(q), len(q), _lib.u64_array(k), len(k), _lib.u64_array(v), len(v),
+                                   C.cast(m, _lib.U64P) if m is not None else None, len(mask) if mask is not None else 0,
+                                   _attn_options(options), out, C.byref(rank)))
+    return [out[i] for i in range(rank.value)]
+
+
+def reduce_shape(op: int, shape: Sequence[int], axes: Sequence[int], keep_dims: bool, mean: bool = False) -> list:
+    """reduction_shape / mean_shape (host only)."""
+    out = (C.c_uint64 * _lib.MAX_RANK)()
+    rank = C.c_uint32()
+    _check(lib().fb_reduce_shape(int(op), _lib.u64_array(shape), len(shape), _lib.u32_array(axes), len(axes),
+                                 int(keep_dims), int(mean), out, C.byref(rank)))
+    return [out[i] for i in range(rank.value)]
+
+
+# ----------------------------------------------------------- convolution
+
+def _conv(fn, input, weight, options, out_dtype):
+    dev = _device(input, weight)
+    opts, _keep = _conv_options(options)
+    dims = conv_plan(list(input.shape), list(weight.shape), options) if True else None
+    out = torch.empty(dims, dtype=out_dtype, device=dev)
+    di, dw, do = describe(input), describe(weight), describe(out)
+    _check(fn(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    return out
+
+
+def conv(input: torch.Tensor, weight: torch.Tensor, options: ConvOptions) -> torch.Tensor:
+    """f32 cross-correlation, bit-identical to the reference kernel's f32 arithmetic."""
+    return _conv(lib().fb_conv, input, weight, options, torch.float32)
+
+
+def conv_low_f32(input: torch.Tensor, weight: torch.Tensor, options: ConvOptions) -> torch.Tensor:
+    """f16/bf16 operands, f32 accumulation and output."""
+    return _conv(lib().fb_conv_low_f32, input, weight, options, torch.float32)
+
+
+def conv_low(input: torch.Tensor, weight: torch.Tensor, options: ConvOptions) -> torch.Tensor:
+    """conv_low_f32 rounded once (nearest-even) to the input dtype."""
+    return _conv(lib().fb_conv_low, input, weight, options, input.dtype)
+
+
+def conv_low_f32_into(input, weight, options, out):
+    """conv_low_f32 into a caller-provided output view (e.g. a channels-last permuted view)."""
+    dev = _device(input, weight)
+    opts, _keep = _conv_options(options)
+    di, dw, do = describe(input), describe(weight), describe(out)
+    _check(lib().fb_conv_low_f32(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    return out
+
+
+# ------------------------------------------------------------- attention
+
+def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions):
+    dev = _device(query, key, value)
+    kind = 0
+    dm = None
+    if mask is not None:
+        kind = {"keep": 1, "additive": 2}[mask.kind]
+    dims = attention_plan(list(query.shape), list(key.shape), list(value.shape),
+                          list(mask.tensor.shape) if mask is not None else None, options)
+    out = torch.empty(dims, dtype=torch.float32, device=dev)
+    dq, dk, dv, do = describe(query), describe(key), describe(value), describe(out)
+    if mask is not None:
+        dm = describe(mask.tensor)
+        if mask.kind == "keep":
+            dm.dtype = _lib.U32
+    _check(fn(C.byref(dq), C.byref(dk), C.byref(dv), kind, C.byref(dm) if dm is not None else None,
+              _attn_options(options), C.byref(do), _stream(dev)))
+    return out
+
+
+def attention(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):
+    """softmax(scale * Q K^T + mask) V for f32 operands."""
+    return _attention(lib().fb_attention, query, key, value, mask, options)
+
+
+def attention_low_f32(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):
+    """Attention from f16/bf16 operands with f32 output."""
+    return _attention(lib().fb_attention_low_f32, query, key, value, mask, options)
+
+
+# ------------------------------------------------------------- reductions
+
+def _reduce(fn, op, input, axes, keep_dims, mean, out_dtype):
+    dev = _device(input)
+    dims = reduce_shape(op, list(input.shape), axes, keep_dims, mean)
+    out = torch.empty(dims, dtype=out_dtype, device=dev)
+    di, do = describe(input), describe(out)
+    if out_dtype == torch.int32:
+        do.dtype = _lib.U32
+        if input.dtype == torch.int32:
+            di.dtype = _lib.U32
+    ax = _lib.u32_array(axes)
+    if mean:
+        _check(fn(C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+    else:
+        _check(fn(int(op), C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+    return out
+
+
+def reduce_f32(op: ReduceOp, input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> torch.Tensor:
+    return _reduce(lib().fb_reduce_f32, op, input, list(axes), keep_dims, False, torch.float32)
+
+
+def reduce_u32(op: ReduceOp, input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> torch.Tensor:
+    """u32 reduction; u32 data is carried in int32 tensors (same bits)."""
+    return _reduce(lib().fb_reduce_u32, op, input, list(axes), keep_dims, False, torch.int32)
+
+
+def mean_axes(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> torch.Tensor:
+    return _reduce(lib().fb_mean_axes, ReduceOp.Sum, input, list(axes), keep_dims, True, torch.float32)
+
+
+def argmax(input: torch.Tensor, axis: int, keep_dims: bool = False) -> torch.Tensor:
+    """Index of the maximum along ``axis`` (total order, lowest index on ties), as int32 holding u32."""
+    dev = _device(input)
+    dims = reduce_shape(ReduceOp.Max, list(input.shape), [axis], keep_dims)
+    out = torch.empty(dims, dtype=torch.int32, device=dev)
+    di, do = describe(input), describe(out)
+    do.dtype = _lib.U32
+    _check(lib().fb_argmax(C.byref(di), axis, int(keep_dims), C.byref(do), _stream(dev)))
+    return out
+
+
+def sum_partial_f64(input: torch.Tensor, partial: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """f64 sum of every element, left on the device (one-element float64 tensor)."""
+    dev = _device(input)
+    if partial is None:
+        partial = torch.empty((), dtype=torch.float64, device=dev)
+    di = describe(input)
+    _check(lib().fb_sum_partial_f64(C.byref(di), C.c_void_p(partial.data_ptr()), _stream(dev)))
+    return partial
+
+
+def finish_sum(partial: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    dev = _device(partial)
+    if out is None:
+        out = torch.empty((), dtype=torch.float32, device=dev)
+    do = describe(out)
+    _check(lib().fb_finish_sum_f64(C.c_void_p(partial.data_ptr()), C.byref(do), _stream(dev)))
+    return out
+
+
+def global_sum(shard: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum over all elements of all ranks' shards: local f64 partial, one
+    all-reduce of 8 bytes when a process group is given, then f32 rounding."""
+    partial = sum_partial_f64(shard)
+    if group is not None or (torch.distributed.is_available() and torch.distributed.is_initialized()):
+        torch.distributed.all_reduce(partial, group=group)
+    return finish_sum(partial)
+
+
+# ------------------------------------------------------------- statistics
+
+def _normalize(fn, input, axes, eps=None):
+    dev = _device(input)
+    out = torch.empty(list(input.shape), dtype=torch.float32, device=dev)
+    di, do = describe(input), describe(out)
+    ax = _lib.u32_array(axes)
+    if eps is None:
+        _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev)))
+    else:
+        _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev)))
+    return out
+
+
+def softmax(input: torch.Tensor, axes: Sequence[int]) -> torch.Tensor:
+    return _normalize(lib().fb_softmax, input, list(axes))
+
+
+def log_softmax(input: torch.Tensor, axes: Sequence[int]) -> torch.Tensor:
+    return _normalize(lib().fb_log_softmax, input, list(axes))
+
+
+def layer_norm(input: torch.Tensor, axes: Sequence[int], epsilon: float) -> torch.Tensor:
+    return _normalize(lib().fb_layer_norm, input, list(axes), float(epsilon))
+
+
+def logsumexp(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> torch.Tensor:
+    dev = _device(input)
+    dims = reduce_shape(ReduceOp.Sum, list(input.shape), list(axes), keep_dims, True)
+    out = torch.empty(dims, dtype=torch.float32, device=dev)
+    di, do = describe(input), describe(out)
+    _check(lib().fb_logsumexp(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+    return out
+
+
+def moments(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> Moments:
+    dev = _device(input)
+    dims = reduce_shape(ReduceOp.Sum, list(input.shape), list(axes), keep_dims, True)
+    mean = torch.empty(dims, dtype=torch.float32, device=dev)
+    var = torch.empty(dims, dtype=torch.float32, device=dev)
+    di, dm, dv = describe(input), describe(mean), describe(var)
+    _check(lib().fb_moments(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(dm), C.byref(dv),
+                            _stream(dev)))
+    return Moments(mean, var)
+
+
+# low-storage statistics are the same calls with f16/bf16 inputs
+softmax_low_f32 = softmax
+log_softmax_low_f32 = log_softmax
+layer_norm_low_f32 = layer_norm
+logsumexp_low_f32 = logsumexp
+moments_low_f32 = moments
+
+
+def cast_to_low(input: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    dev = _device(input)
+    out = torch.empty(list(input.shape), dtype=dtype, device=dev)
+    di, do = describe(input), describe(out)
+    _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(dev)))
+    return out
+
+
+def launch_count() -> int:
+    """Kernel launches this library has enqueued."""
+    return int(lib().fb_launch_count())

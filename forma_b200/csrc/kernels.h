@@ -1,0 +1,140 @@
+// Launch interface between the C ABI (api.cpp) and the CUDA translation
+// units.  Everything here is plain data: the ABI layer validates and
+// canonicalises descriptors, the launchers only enqueue work.
+#pragma once
+
+#include <cstdint>
+
+#include "../../include/forma_b200.h"
+
+namespace fb {
+
+// An index nest: logical row-major coordinates over `dims` mapped to an
+// element offset through `strides` (the reference's index_of walk,
+// compute-cuda/src/kernels.cu:5-13, with the dims resident in kernel
+// parameters instead of an uploaded u64 descriptor).
+struct Nest {
+    uint32_t rank = 0;
+    uint64_t dims[FB_MAX_RANK] = {};
+    uint64_t strides[FB_MAX_RANK] = {};
+};
+
+// A row-structured view of a reduction or statistics operand: row r, column
+// c lives at `offset + outer(r) + inner(c)`.  When `contiguous_rows` is set
+// the inner nest is one stride-1 axis of `cols` elements and the outer nest
+// one axis of stride `row_stride`.
+struct Rows {
+    const void* data = nullptr;
+    uint32_t dtype = FB_F32;
+    uint64_t offset = 0;
+    uint64_t rows = 0, cols = 0;
+    Nest outer, inner;
+    bool contiguous_rows = false;
+    uint64_t row_stride = 0;
+};
+
+// Destination of one value per row (reductions, logsumexp, moments).
+struct RowOut {
+    void* data = nullptr;
+    uint64_t offset = 0;
+    Nest nest;  // over rows
+    bool contiguous = false;
+};
+
+// Destination with the input's geometry (softmax, log-softmax, layer norm).
+struct ElemOut {
+    float* data = nullptr;
+    uint64_t offset = 0;
+    Nest outer, inner;
+    bool contiguous_rows = false;
+    uint64_t row_stride = 0;
+};
+
+enum RowOp : uint32_t {
+    ROW_SUM = 0,
+    ROW_PRODUCT = 1,
+    ROW_MIN = 2,
+    ROW_MAX = 3,
+    ROW_MEAN = 4,
+    ROW_ARGMAX = 5,
+};
+
+enum StatsOp : uint32_t {
+    STATS_SOFTMAX = 0,
+    STATS_LOG_SOFTMAX = 1,
+    STATS_LAYER_NORM = 2,
+    STATS_LOGSUMEXP = 3,
+    STATS_MOMENTS = 4,
+};
+
+// Library-owned scratch for the calling (device, stream) pair; grows on
+// demand and lives until process exit.  Returns nullptr on allocation failure.
+void* scratch(void* stream, uint64_t bytes);
+int sm_count();
+void count_launch();
+
+// ---- reductions / statistics (reduce.cu) ----
+int launch_reduce_rows(uint32_t op, const Rows& in, const RowOut& out, void* stream);
+int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const RowOut& out_a, const RowOut& out_b,
+                      float epsilon, void* stream);
+int launch_sum_partial(const Rows& in, double* partial, void* stream);
+int launch_finish_sum(const double* partial, float* out, void* stream);
+// Writes `count` elements of `value` (f32 or u32 bits) into a dense-permuted output.
+int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream);
+// Copies a strided view into a (dense-permuted) output of the same logical shape.
+int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const Nest& in_nest, void* out,
+                uint64_t out_offset, const Nest& out_nest, uint64_t count, void* stream);
+// Rounds f32 (strided) into F16/BF16 contiguous storage, nearest-even.
+int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest, uint16_t* out, uint32_t dtype,
+                       uint64_t count, void* stream);
+
+// ---- convolution (conv_simt.cu, conv_tc.cu) ----
+struct ConvArgs {
+    const void* input = nullptr;
+    const void* weight = nullptr;
+    float* output = nullptr;
+    uint32_t dtype = FB_F32;  // input/weight dtype
+    uint32_t spatial = 0;
+    uint64_t in_offset = 0, w_offset = 0, out_offset = 0;
+    uint64_t batch = 0, channels_per_group = 0, outputs_per_group = 0, out_channels = 0;
+    uint64_t in_stride_n = 0, in_stride_c = 0, w_stride_o = 0, w_stride_c = 0;
+    uint64_t out_stride_n = 0, out_stride_c = 0;
+    uint64_t in_dims[3] = {1, 1, 1}, out_dims[3] = {1, 1, 1}, k_dims[3] = {1, 1, 1};
+    uint64_t in_strides[3] = {0, 0, 0}, w_strides[3] = {0, 0, 0}, out_strides[3] = {0, 0, 0};
+    uint64_t stride[3] = {1, 1, 1}, dilation[3] = {1, 1, 1}, pad[3] = {0, 0, 0};
+    uint64_t out_count = 0;
+};
+int launch_conv_direct(const ConvArgs& a, void* stream);
+// Returns FB_ERR_UNSUPPORTED when the geometry has no tiled kernel.
+int launch_conv2d_f32_tiled(const ConvArgs& a, void* stream);
+int launch_conv_tc(const ConvArgs& a, void* stream);
+
+// ---- attention (attention_simt.cu, attention_tc.cu) ----
+struct AttnArgs {
+    const void* q = nullptr;
+    const void* k = nullptr;
+    const void* v = nullptr;
+    const void* mask = nullptr;
+    float* out = nullptr;
+    uint32_t dtype = FB_F32;
+    uint32_t mask_kind = FB_MASK_NONE;
+    // Row nest over [batch..., heads, queries] with per-operand strides; K/V
+    // strides on the query axis are zero and their head coordinate is the
+    // query head divided by `group_size`.
+    uint32_t row_rank = 0;
+    uint64_t row_dims[FB_MAX_RANK] = {};
+    uint64_t q_row_strides[FB_MAX_RANK] = {}, k_row_strides[FB_MAX_RANK] = {};
+    uint64_t v_row_strides[FB_MAX_RANK] = {}, m_row_strides[FB_MAX_RANK] = {};
+    uint64_t o_row_strides[FB_MAX_RANK] = {};
+    uint64_t q_offset = 0, k_offset = 0, v_offset = 0, m_offset = 0, o_offset = 0;
+    uint64_t q_stride_d = 0, k_stride_key = 0, k_stride_d = 0, v_stride_key = 0, v_stride_d = 0;
+    uint64_t m_stride_key = 0, o_stride_d = 0;
+    uint64_t rows = 0, keys = 0, depth = 0, value_depth = 0, group_size = 1;
+    float scale = 1.0f;
+    bool causal = false;
+    int32_t causal_offset = 0;
+};
+int launch_attention_simt(const AttnArgs& a, void* stream);
+int launch_attention_tc(const AttnArgs& a, void* stream);
+
+}  // namespace fb

@@ -1,0 +1,452 @@
+// Row reductions, argmax, statistics and the global-sum partial.
+//
+// Every operation is a pass over "rows" (the kept coordinates) of "columns"
+// (the contracted coordinates).  One 256-thread block owns a row at a time
+// and the grid strides over rows, sized to a multiple of the SM count.  For
+// the dominant case - contiguous rows of an f32 matrix - columns are read
+// with 128-bit loads, several in flight per thread, and statistics keep the
+// whole row in registers so softmax and layer norm read HBM once and write
+// once (the reference reads the input three times and keeps f64 partials in
+// global memory: compute-cuda/src/statistics.cu:139-208).  Other layouts use
+// the same kernels with per-element nest addressing.
+//
+// Arithmetic: sums, products and moments accumulate in f64; min, max and
+// argmax compare total-order keys so they are exact and order-independent.
+#include <cuda_runtime.h>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace fb {
+namespace {
+
+constexpr int BLOCK = 256;
+
+template <typename T>
+__device__ __forceinline__ const T* row_base(const Rows& in, uint64_t row) {
+    const T* p = reinterpret_cast<const T*>(in.data) + in.offset;
+    return p + (in.contiguous_rows ? row * in.row_stride : nest_offset(in.outer, row));
+}
+
+template <typename T>
+__device__ __forceinline__ float row_elem(const Rows& in, const T* base, uint64_t c) {
+    return Elem<T>::load(base + (in.contiguous_rows ? c : nest_offset(in.inner, c)));
+}
+
+__device__ __forceinline__ uint64_t out_index(const RowOut& o, uint64_t row) {
+    return o.offset + (o.contiguous ? row : nest_offset(o.nest, row));
+}
+
+__device__ __forceinline__ float* elem_out(const ElemOut& o, uint64_t row, uint64_t c) {
+    if (o.contiguous_rows) return o.data + o.offset + row * o.row_stride + c;
+    return o.data + o.offset + nest_offset(o.outer, row) + nest_offset(o.inner, c);
+}
+
+// Per-thread state of one reduction.
+struct Acc {
+    double sum;
+    uint64_t best;  // (key << 32) | (0xffffffff - column): max = largest key, lowest column
+};
+
+__device__ __forceinline__ void acc_add(Acc& a, uint32_t op, float x, uint64_t c) {
+    if (op == ROW_SUM || op == ROW_MEAN) {
+        a.sum += (double)x;
+    } else if (op == ROW_PRODUCT) {
+        a.sum *= (double)x;
+    } else {
+        uint32_t k = order_key(x);
+        if (op == ROW_MIN) k = ~k;
+        const uint64_t packed = ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)c);
+        a.best = packed > a.best ? packed : a.best;
+    }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(BLOCK) reduce_rows_kernel(Rows in, RowOut out, uint32_t op) {
+    __shared__ double s_sum[BLOCK / 32];
+    __shared__ uint64_t s_best[BLOCK / 32];
+    __shared__ double s_prod[BLOCK];
+    for (uint64_t row = blockIdx.x; row < in.rows; row += gridDim.x) {
+        const T* base = row_base<T>(in, row);
+        Acc a{op == ROW_PRODUCT ? 1.0 : 0.0, 0};
+        uint64_t c0 = 0;
+        if (VEC == 4) {
+            // 128-bit (f32) or 64-bit (low) loads, four vectors in flight.
+            const uint64_t nvec = in.cols / 4;
+            uint64_t v = threadIdx.x;
+            for (; v + 3 * BLOCK < nvec; v += 4 * BLOCK) {
+                float4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) x[u] = Elem<T>::load4(base + (v + u * BLOCK) * 4);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint64_t c = (v + u * BLOCK) * 4;
+                    acc_add(a, op, x[u].x, c);
+                    acc_add(a, op, x[u].y, c + 1);
+                    acc_add(a, op, x[u].z, c + 2);
+                    acc_add(a, op, x[u].w, c + 3);
+                }
+            }
+            for (; v < nvec; v += BLOCK) {
+                const float4 x = Elem<T>::load4(base + v * 4);
+                acc_add(a, op, x.x, v * 4);
+                acc_add(a, op, x.y, v * 4 + 1);
+                acc_add(a, op, x.z, v * 4 + 2);
+                acc_add(a, op, x.w, v * 4 + 3);
+            }
+            c0 = nvec * 4;
+        }
+        for (uint64_t c = c0 + threadIdx.x; c < in.cols; c += BLOCK) acc_add(a, op, row_elem<T>(in, base, c), c);
+
+        if (op == ROW_PRODUCT) {
+            // Products have no warp shuffle identity worth special-casing: a
+            // shared-memory tree in fixed order.
+            s_prod[threadIdx.x] = a.sum;
+            __syncthreads();
+            for (int s = BLOCK / 2; s; s >>= 1) {
+                if (threadIdx.x < s) s_prod[threadIdx.x] *= s_prod[threadIdx.x + s];
+                __syncthreads();
+            }
+            if (threadIdx.x == 0) static_cast<float*>(out.data)[out_index(out, row)] = (float)s_prod[0];
+            __syncthreads();
+        } else if (op == ROW_SUM || op == ROW_MEAN) {
+            const double t = block_sum<BLOCK>(a.sum, s_sum);
+            if (threadIdx.x == 0)
+                static_cast<float*>(out.data)[out_index(out, row)] =
+                    op == ROW_MEAN ? (float)(t / (double)in.cols) : (float)t;
+        } else {
+            const uint64_t b = block_max_u64<BLOCK>(a.best, s_best);
+            if (threadIdx.x == 0) {
+                uint32_t k = (uint32_t)(b >> 32);
+                if (op == ROW_ARGMAX)
+                    static_cast<uint32_t*>(out.data)[out_index(out, row)] = 0xffffffffu - (uint32_t)(b & 0xffffffffu);
+                else
+                    static_cast<float*>(out.data)[out_index(out, row)] = key_value(op == ROW_MIN ? ~k : k);
+            }
+        }
+    }
+}
+
+// u32 reductions (TensorReduceBackend::reduce_u32): wrapping sum/product.
+__global__ void __launch_bounds__(BLOCK) reduce_rows_u32_kernel(Rows in, RowOut out, uint32_t op) {
+    __shared__ uint32_t s[BLOCK];
+    for (uint64_t row = blockIdx.x; row < in.rows; row += gridDim.x) {
+        const uint32_t* base = reinterpret_cast<const uint32_t*>(in.data) + in.offset +
+                               (in.contiguous_rows ? row * in.row_stride : nest_offset(in.outer, row));
+        uint32_t a = op == ROW_PRODUCT ? 1u : (op == ROW_MIN ? 0xffffffffu : 0u);
+        for (uint64_t c = threadIdx.x; c < in.cols; c += BLOCK) {
+            const uint32_t x = __ldg(base + (in.contiguous_rows ? c : nest_offset(in.inner, c)));
+            a = op == ROW_SUM ? a + x : op == ROW_PRODUCT ? a * x : op == ROW_MIN ? min(a, x) : max(a, x);
+        }
+        s[threadIdx.x] = a;
+        __syncthreads();
+        for (int w = BLOCK / 2; w; w >>= 1) {
+            if (threadIdx.x < w) {
+                const uint32_t x = s[threadIdx.x], y = s[threadIdx.x + w];
+                s[threadIdx.x] = op == ROW_SUM ? x + y : op == ROW_PRODUCT ? x * y : op == ROW_MIN ? min(x, y) : max(x, y);
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) static_cast<uint32_t*>(out.data)[out_index(out, row)] = s[0];
+        __syncthreads();
+    }
+}
+
+// Statistics over rows (TensorStatsBackend).  NV > 0 keeps the row in
+// registers: NV float4 per thread, so rows of up to 4*NV*BLOCK columns are read
+// from HBM exactly once and written once with 128-bit stores (input and output
+// rows contiguous and 16-byte aligned).  NV == 0 re-reads the row from memory
+// for each pass and addresses any strided layout.
+//   softmax      exp(x - max) / sum exp(x - max)
+//   log-softmax  (x - max) - log(sum)
+//   logsumexp    max + log(sum)
+//   moments      mean = sum x / n, var = sum (x - mean)^2 / n (f64, centred)
+//   layer norm   (x - mean) / sqrt(var + eps)
+// exp is CUDA's expf on the f32 shift, as in compute-cuda/src/statistics.cu:151;
+// every sum is f64.
+template <typename T, int NV>
+__global__ void __launch_bounds__(BLOCK) stats_rows_kernel(Rows in, ElemOut out, RowOut oa, RowOut ob, uint32_t op,
+                                                           float eps) {
+    __shared__ double s_sum[BLOCK / 32];
+    __shared__ float s_max[BLOCK / 32];
+    const bool exp_family = op == STATS_SOFTMAX || op == STATS_LOG_SOFTMAX || op == STATS_LOGSUMEXP;
+    for (uint64_t row = blockIdx.x; row < in.rows; row += gridDim.x) {
+        const T* base = row_base<T>(in, row);
+        const uint64_t n = in.cols;
+        float4 cache[NV > 0 ? NV : 1];
+        if constexpr (NV > 0) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const uint64_t v = threadIdx.x + (uint64_t)j * BLOCK;
+                cache[j] = v * 4 < n ? Elem<T>::load4(base + v * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        // Applies f to every element this thread owns.
+        auto each = [&](auto&& f) {
+            if constexpr (NV > 0) {
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    if ((threadIdx.x + (uint64_t)j * BLOCK) * 4 < n) {
+                        f(cache[j].x);
+                        f(cache[j].y);
+                        f(cache[j].z);
+                        f(cache[j].w);
+                    }
+                }
+            } else {
+                for (uint64_t c = threadIdx.x; c < n; c += BLOCK) f(row_elem<T>(in, base, c));
+            }
+        };
+        // Writes g(x) for every element this thread owns.
+        auto emit = [&](auto&& g) {
+            if constexpr (NV > 0) {
+                float* orow = out.data + out.offset + row * out.row_stride;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    const uint64_t c = (threadIdx.x + (uint64_t)j * BLOCK) * 4;
+                    if (c < n)
+                        *reinterpret_cast<float4*>(orow + c) =
+                            make_float4(g(cache[j].x), g(cache[j].y), g(cache[j].z), g(cache[j].w));
+                }
+            } else {
+                for (uint64_t c = threadIdx.x; c < n; c += BLOCK) *elem_out(out, row, c) = g(row_elem<T>(in, base, c));
+            }
+        };
+        if (exp_family) {
+            float m = -__int_as_float(0x7f800000);
+            each([&](float x) { m = fmaxf(m, x); });
+            m = block_max<BLOCK>(m, s_max);
+            double s = 0.0;
+            each([&](float x) { s += (double)expf(x - m); });
+            s = block_sum<BLOCK>(s, s_sum);
+            if (op == STATS_SOFTMAX) {
+                const double inv = 1.0 / s;
+                emit([&](float x) { return (float)((double)expf(x - m) * inv); });
+            } else if (op == STATS_LOG_SOFTMAX) {
+                const double shift = (double)m + log(s);
+                emit([&](float x) { return (float)((double)x - shift); });
+            } else if (threadIdx.x == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(s));
+            }
+        } else {
+            double s = 0.0;
+            each([&](float x) { s += (double)x; });
+            const double mean = block_sum<BLOCK>(s, s_sum) / (double)n;
+            double q = 0.0;
+            each([&](float x) {
+                const double d = (double)x - mean;
+                q += d * d;
+            });
+            const double var = block_sum<BLOCK>(q, s_sum) / (double)n;
+            if (op == STATS_LAYER_NORM) {
+                const double inv = 1.0 / sqrt(var + (double)eps);
+                emit([&](float x) { return (float)(((double)x - mean) * inv); });
+            } else if (threadIdx.x == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
+                static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
+            }
+        }
+    }
+}
+
+// Global f32 sum into one f64: grid-stride f64 partials per block, then the
+// last block to finish folds the block partials in index order (so the
+// result does not depend on block scheduling) and re-arms the counter.
+template <int VEC>
+__global__ void __launch_bounds__(BLOCK) sum_partial_kernel(Rows in, double* block_partials, unsigned* counter,
+                                                            double* result) {
+    __shared__ double s_sum[BLOCK / 32];
+    __shared__ bool s_last;
+    const float* base = reinterpret_cast<const float*>(in.data) + in.offset;
+    const uint64_t n = in.cols;
+    double acc = 0.0;
+    const uint64_t tid = (uint64_t)blockIdx.x * BLOCK + threadIdx.x, step = (uint64_t)gridDim.x * BLOCK;
+    uint64_t c0 = 0;
+    if (VEC == 4) {
+        const uint64_t nvec = n / 4;
+        uint64_t v = tid;
+        for (; v + 3 * step < nvec; v += 4 * step) {
+            float4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = Elem<float>::load4(base + (v + u * step) * 4);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc += ((double)x[u].x + (double)x[u].y) + ((double)x[u].z + (double)x[u].w);
+        }
+        for (; v < nvec; v += step) {
+            const float4 x = Elem<float>::load4(base + v * 4);
+            acc += ((double)x.x + (double)x.y) + ((double)x.z + (double)x.w);
+        }
+        c0 = nvec * 4;
+    }
+    for (uint64_t c = c0 + tid; c < n; c += step)
+        acc += (double)Elem<float>::load(base + (in.contiguous_rows ? c : nest_offset(in.inner, c)));
+    acc = block_sum<BLOCK>(acc, s_sum);
+    if (threadIdx.x == 0) {
+        block_partials[blockIdx.x] = acc;
+        __threadfence();
+        s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        double t = 0.0;
+        for (unsigned b = threadIdx.x; b < gridDim.x; b += BLOCK) t += __ldcg(block_partials + b);
+        t = block_sum<BLOCK>(t, s_sum);
+        if (threadIdx.x == 0) {
+            *result = t;
+            *counter = 0u;
+        }
+    }
+}
+
+__global__ void finish_sum_kernel(const double* partial, float* out) { *out = (float)*partial; }
+
+__global__ void fill_kernel(uint32_t* out, uint64_t count, uint32_t bits) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = bits;
+}
+
+template <typename E>
+__global__ void copy_kernel(const E* in, uint64_t in_offset, Nest in_nest, E* out, uint64_t out_offset, Nest out_nest,
+                            uint64_t count) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+        out[out_offset + nest_offset(out_nest, i)] = in[in_offset + nest_offset(in_nest, i)];
+}
+
+__global__ void cast_to_low_kernel(const float* in, uint64_t in_offset, Nest in_nest, uint16_t* out, uint32_t dtype,
+                                   uint64_t count) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float x = in[in_offset + nest_offset(in_nest, i)];
+        out[i] = dtype == FB_BF16 ? encode_bf16(x) : encode_f16(x);
+    }
+}
+
+unsigned grid_for(uint64_t work, unsigned per_sm = 8) {
+    const uint64_t cap = (uint64_t)sm_count() * per_sm;
+    uint64_t g = work < cap ? work : cap;
+    return (unsigned)(g ? g : 1);
+}
+
+int check_launch() {
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+}
+
+bool vec_ok(const Rows& in) {
+    if (!in.contiguous_rows) return false;
+    const uint64_t esz = in.dtype == FB_F32 || in.dtype == FB_U32 ? 4 : 2;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(in.data) + in.offset * esz;
+    return addr % (4 * esz) == 0 && (in.rows <= 1 || in.row_stride % 4 == 0);
+}
+
+template <typename T>
+int reduce_typed(uint32_t op, const Rows& in, const RowOut& out, cudaStream_t s) {
+    const unsigned g = grid_for(in.rows);
+    if (vec_ok(in))
+        reduce_rows_kernel<T, 4><<<g, BLOCK, 0, s>>>(in, out, op);
+    else
+        reduce_rows_kernel<T, 1><<<g, BLOCK, 0, s>>>(in, out, op);
+    return check_launch();
+}
+
+template <typename T>
+int stats_typed(uint32_t op, const Rows& in, const ElemOut& out, const RowOut& a, const RowOut& b, float eps,
+                cudaStream_t s) {
+    const unsigned g = grid_for(in.rows);
+    const bool elementwise = op == STATS_SOFTMAX || op == STATS_LOG_SOFTMAX || op == STATS_LAYER_NORM;
+    const bool out_ok = !elementwise ||
+                        (out.contiguous_rows && reinterpret_cast<uintptr_t>(out.data + out.offset) % 16 == 0 &&
+                         (in.rows <= 1 || out.row_stride % 4 == 0));
+    const bool cache = vec_ok(in) && in.cols % 4 == 0 && out_ok;
+    const uint64_t per_pass = 4ull * BLOCK;
+    if (cache && in.cols <= per_pass)
+        stats_rows_kernel<T, 1><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
+    else if (cache && in.cols <= 2 * per_pass)
+        stats_rows_kernel<T, 2><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
+    else if (cache && in.cols <= 4 * per_pass)
+        stats_rows_kernel<T, 4><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
+    else if (cache && in.cols <= 8 * per_pass)
+        stats_rows_kernel<T, 8><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
+    else
+        stats_rows_kernel<T, 0><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
+    return check_launch();
+}
+
+}  // namespace
+
+int launch_reduce_rows(uint32_t op, const Rows& in, const RowOut& out, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (in.rows == 0) return FB_OK;
+    switch (in.dtype) {
+        case FB_F32: return reduce_typed<float>(op, in, out, s);
+        case FB_BF16: return reduce_typed<__nv_bfloat16>(op, in, out, s);
+        case FB_F16: return reduce_typed<__half>(op, in, out, s);
+        case FB_U32:
+            reduce_rows_u32_kernel<<<grid_for(in.rows), BLOCK, 0, s>>>(in, out, op);
+            return check_launch();
+        default: return FB_ERR_DTYPE;
+    }
+}
+
+int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const RowOut& a, const RowOut& b, float eps,
+                      void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (in.rows == 0) return FB_OK;
+    switch (in.dtype) {
+        case FB_F32: return stats_typed<float>(op, in, out, a, b, eps, s);
+        case FB_BF16: return stats_typed<__nv_bfloat16>(op, in, out, a, b, eps, s);
+        case FB_F16: return stats_typed<__half>(op, in, out, a, b, eps, s);
+        default: return FB_ERR_DTYPE;
+    }
+}
+
+int launch_sum_partial(const Rows& in, double* partial, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned g = (unsigned)sm_count() * 4;
+    // Scratch layout: [g doubles of block partials][one u32 counter].
+    char* scr = static_cast<char*>(scratch(stream, (uint64_t)g * sizeof(double) + 256));
+    if (!scr) return FB_ERR_DRIVER;
+    double* partials = reinterpret_cast<double*>(scr);
+    unsigned* counter = reinterpret_cast<unsigned*>(scr + (uint64_t)g * sizeof(double));
+    if (vec_ok(in))
+        sum_partial_kernel<4><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
+    else
+        sum_partial_kernel<1><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
+    return check_launch();
+}
+
+int launch_finish_sum(const double* partial, float* out, void* stream) {
+    finish_sum_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(partial, out);
+    return check_launch();
+}
+
+int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream) {
+    if (count == 0) return FB_OK;
+    fill_kernel<<<grid_for((count + BLOCK - 1) / BLOCK), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint32_t*>(data), count, bits);
+    return check_launch();
+}
+
+int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const Nest& in_nest, void* out,
+                uint64_t out_offset, const Nest& out_nest, uint64_t count, void* stream) {
+    if (count == 0) return FB_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned g = grid_for((count + BLOCK - 1) / BLOCK);
+    if (elem_bytes == 4)
+        copy_kernel<uint32_t><<<g, BLOCK, 0, s>>>(static_cast<const uint32_t*>(in), in_offset, in_nest,
+                                                  static_cast<uint32_t*>(out), out_offset, out_nest, count);
+    else
+        copy_kernel<uint16_t><<<g, BLOCK, 0, s>>>(static_cast<const uint16_t*>(in), in_offset, in_nest,
+                                                  static_cast<uint16_t*>(out), out_offset, out_nest, count);
+    return check_launch();
+}
+
+int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest, uint16_t* out, uint32_t dtype,
+                       uint64_t count, void* stream) {
+    if (count == 0) return FB_OK;
+    cast_to_low_kernel<<<grid_for((count + BLOCK - 1) / BLOCK), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(
+        in, in_offset, in_nest, out, dtype, count);
+    return check_launch();
+}
+
+}  // namespace fb

@@ -1,0 +1,268 @@
+/*
+ * forma_b200.h - C ABI of the B200 (sm_100a) dense-op backend.
+ *
+ * This library replaces the kernel launches behind Forma's `compute-cuda`
+ * implementations of the tensor-core traits for convolution, scaled
+ * dot-product attention, reductions and statistics.  The Rust side keeps its
+ * planning, owner checks and output allocation; each trait method ends in one
+ * call below with plain descriptors, a caller stream and an int status.
+ *
+ * Conventions (all mirror the reference runtime):
+ *  - A tensor is a strided view into device storage: `dims`, `strides` and
+ *    `offset` are in ELEMENTS (crates/tensor-core/src/layout.rs:6-16); stride 0
+ *    broadcasts.  `storage_len` is the element count of the backing allocation
+ *    and bounds every access (Layout::validate_storage_len, layout.rs:280-289).
+ *  - Outputs are caller-allocated, exclusive and sized by the matching
+ *    `*_plan` / `*_shape` query; every element of the output is written.
+ *  - Validation happens before empty shortcuts (tensor-core/src/convolution.rs:
+ *    119-124); a non-zero status leaves outputs untouched and launches nothing.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream) and is asynchronous, like the reference's single-stream runtime
+ *    (compute-cuda/src/runtime.rs:66-81).
+ *  - There is no CPU fallback: a missing device or kernel is FB_ERR_DRIVER.
+ */
+#ifndef FORMA_B200_H
+#define FORMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FB_MAX_RANK 8
+#define FB_ABI_VERSION 1
+
+/* Element types. F16/BF16 are the reference's LowDtype storage
+ * (tensor-core/src/low_precision.rs:7-10): raw 16-bit patterns. */
+typedef enum fb_dtype {
+    FB_F32 = 0,
+    FB_U32 = 1,
+    FB_F16 = 2,
+    FB_BF16 = 3,
+} fb_dtype;
+
+/* Status codes.  1..31 mirror tensor_core::TensorError
+ * (tensor-core/src/error.rs:1-56); 32.. mirror compute_cuda::CudaError
+ * (compute-cuda/src/error.rs:3-26). */
+typedef enum fb_status {
+    FB_OK = 0,
+    FB_ERR_SHAPE_OVERFLOW = 1,
+    FB_ERR_LAYOUT_OVERFLOW = 2,
+    FB_ERR_RANK_MISMATCH = 3,
+    FB_ERR_AXIS_OUT_OF_BOUNDS = 4,
+    FB_ERR_DUPLICATE_AXIS = 5,
+    FB_ERR_INCOMPATIBLE_BROADCAST = 6,
+    FB_ERR_STORAGE_OUT_OF_BOUNDS = 7,
+    FB_ERR_EMPTY_REDUCTION = 8,
+    FB_ERR_INVALID_EPSILON = 9,
+    FB_ERR_INVALID_ATTENTION = 10,
+    FB_ERR_INVALID_ATTENTION_SCALE = 11,
+    FB_ERR_INVALID_CONVOLUTION = 12,
+    FB_ERR_LOW_DTYPE_MISMATCH = 13,
+    FB_ERR_INVALID_INPUT = 32,
+    FB_ERR_DTYPE = 33,
+    FB_ERR_DRIVER = 34,
+    FB_ERR_UNSUPPORTED = 35,
+} fb_status;
+
+/* Strided view of device storage (compute-cuda/src/runtime.rs:44-61:
+ * CudaTensor = Arc<CudaSlice<T>> + Layout). */
+typedef struct fb_tensor {
+    void* data;           /* device address of storage element 0 */
+    uint64_t storage_len; /* elements in the allocation */
+    uint32_t dtype;       /* fb_dtype */
+    uint32_t rank;        /* 0..FB_MAX_RANK */
+    uint64_t dims[FB_MAX_RANK];
+    uint64_t strides[FB_MAX_RANK];
+    uint64_t offset;
+} fb_tensor;
+
+/* tensor_core::ConvOptions (tensor-core/src/convolution.rs:7-13).  Each vector
+ * has its own length so ConvPlan's "every option vector must match the
+ * spatial rank" check is preserved. */
+typedef struct fb_conv_options {
+    const uint64_t* strides;
+    uint32_t strides_len;
+    const uint64_t* dilations;
+    uint32_t dilations_len;
+    const uint64_t* padding_before;
+    uint32_t padding_before_len;
+    const uint64_t* padding_after;
+    uint32_t padding_after_len;
+    uint64_t groups;
+} fb_conv_options;
+
+/* tensor_core::AttentionOptions (tensor-core/src/attention.rs:3-13). */
+typedef struct fb_attention_options {
+    int32_t has_scale; /* 0 = default 1/sqrt(depth) */
+    float scale;
+    int32_t has_causal; /* 0 = no causal mask */
+    int32_t causal;     /* key j visible to query i iff j <= i + causal */
+} fb_attention_options;
+
+/* tensor_core::AttentionMask (tensor-core/src/attention.rs:15-23). */
+typedef enum fb_mask_kind {
+    FB_MASK_NONE = 0,
+    FB_MASK_KEEP = 1,     /* u32 tensor, nonzero keeps the key */
+    FB_MASK_ADDITIVE = 2, /* f32 tensor, finite bias or -inf */
+} fb_mask_kind;
+
+/* tensor_core::ReduceOp (tensor-core/src/reduction.rs:6-13). */
+typedef enum fb_reduce_op {
+    FB_REDUCE_SUM = 0,
+    FB_REDUCE_PRODUCT = 1,
+    FB_REDUCE_MIN = 2,
+    FB_REDUCE_MAX = 3,
+} fb_reduce_op;
+
+/* ---------------------------------------------------------------- library */
+
+/* FB_ABI_VERSION of the loaded library. */
+int fb_abi_version(void);
+/* Static description of a status code. */
+const char* fb_status_string(int status);
+/* Detail of the last non-zero status returned on this host thread. */
+const char* fb_last_error(void);
+/* Number of kernel launches this library has enqueued (all threads). */
+uint64_t fb_launch_count(void);
+
+/* ------------------------------------------------------------ convolution */
+
+/* ConvPlan::new (tensor-core/src/convolution.rs:43-111): writes the output
+ * dims [N, O, *spatial] and rank.  Host only. */
+int fb_conv_plan(const uint64_t* input_dims, uint32_t input_rank,
+                 const uint64_t* weight_dims, uint32_t weight_rank,
+                 const fb_conv_options* options, uint64_t* out_dims,
+                 uint32_t* out_rank);
+
+/* TensorConvBackend::conv (tensor-core/src/convolution.rs:125-132; replaces
+ * the conv_f32 launch at compute-cuda/src/convolution.rs:180-212).  f32
+ * input/weight/output.  Every output element is accumulated in f32 in the
+ * reference's (input channel, kernel tap) order with separately rounded
+ * multiply and add, so results are bit-identical to the reference kernel. */
+int fb_conv(const fb_tensor* input, const fb_tensor* weight,
+            const fb_conv_options* options, fb_tensor* output, void* stream);
+
+/* TensorLowConvBackend::conv_low_f32 (tensor-core/src/low_convolution.rs:
+ * 16-33; replaces the conv_low launch at compute-cuda/src/convolution.rs:
+ * 226-239).  F16/BF16 input and weight of the same dtype, f32 output.
+ * Channels-last input ([N,C,H,W] viewed over NHWC storage) and weights over
+ * [O,kh,kw,C] storage run as a tcgen05 implicit GEMM with f32 accumulation;
+ * other layouts run a CUDA-core direct kernel with f32 accumulation. */
+int fb_conv_low_f32(const fb_tensor* input, const fb_tensor* weight,
+                    const fb_conv_options* options, fb_tensor* output,
+                    void* stream);
+
+/* TensorLowConvBackend::conv_low (tensor-core/src/low_convolution.rs:35-44):
+ * conv_low_f32 followed by one nearest-even rounding to the input dtype.
+ * `output` has the input's low dtype. */
+int fb_conv_low(const fb_tensor* input, const fb_tensor* weight,
+                const fb_conv_options* options, fb_tensor* output,
+                void* stream);
+
+/* -------------------------------------------------------------- attention */
+
+/* AttentionPlan::new (tensor-core/src/attention.rs:82-170): output dims and
+ * rank.  `mask_dims` may be NULL when there is no mask.  Host only. */
+int fb_attention_plan(const uint64_t* q_dims, uint32_t q_rank,
+                      const uint64_t* k_dims, uint32_t k_rank,
+                      const uint64_t* v_dims, uint32_t v_rank,
+                      const uint64_t* mask_dims, uint32_t mask_rank,
+                      fb_attention_options options, uint64_t* out_dims,
+                      uint32_t* out_rank);
+
+/* TensorAttentionBackend::attention (tensor-core/src/attention.rs:49-58;
+ * replaces the attention_f32 launch at compute-cuda/src/attention.rs:20-81).
+ * f32 Q/K/V; `mask` is NULL for FB_MASK_NONE. */
+int fb_attention(const fb_tensor* query, const fb_tensor* key,
+                 const fb_tensor* value, uint32_t mask_kind,
+                 const fb_tensor* mask, fb_attention_options options,
+                 fb_tensor* output, void* stream);
+
+/* TensorLowAttentionBackend::attention_low_f32 (tensor-core/src/
+ * low_attention.rs:28-49; replaces compute-cuda/src/low_attention.rs:4-28).
+ * F16/BF16 Q/K/V of one dtype, f32 output.  Dense [..., L, D] heads with
+ * D in {64, 128} and no mask tensor run as a fused tcgen05 flash kernel;
+ * other geometries run a CUDA-core online-softmax kernel. */
+int fb_attention_low_f32(const fb_tensor* query, const fb_tensor* key,
+                         const fb_tensor* value, uint32_t mask_kind,
+                         const fb_tensor* mask, fb_attention_options options,
+                         fb_tensor* output, void* stream);
+
+/* -------------------------------------------------------------- reduction */
+
+/* reduction_shape / mean_shape (tensor-core/src/reduction.rs:44-72). */
+int fb_reduce_shape(uint32_t op, const uint64_t* dims, uint32_t rank,
+                    const uint32_t* axes, uint32_t n_axes, int32_t keep_dims,
+                    int32_t is_mean, uint64_t* out_dims, uint32_t* out_rank);
+
+/* TensorReduceBackend::reduce_f32 (tensor-core/src/reduction.rs:20-27;
+ * replaces compute-cuda/src/reduction.rs:79-160). */
+int fb_reduce_f32(uint32_t op, const fb_tensor* input, const uint32_t* axes,
+                  uint32_t n_axes, int32_t keep_dims, fb_tensor* output,
+                  void* stream);
+
+/* TensorReduceBackend::reduce_u32 (tensor-core/src/reduction.rs:28-34):
+ * wrapping sum/product, exact min/max. */
+int fb_reduce_u32(uint32_t op, const fb_tensor* input, const uint32_t* axes,
+                  uint32_t n_axes, int32_t keep_dims, fb_tensor* output,
+                  void* stream);
+
+/* TensorReduceBackend::mean_axes (tensor-core/src/reduction.rs:35-40;
+ * replaces compute-cuda/src/reduction.rs:205-224). */
+int fb_mean_axes(const fb_tensor* input, const uint32_t* axes,
+                 uint32_t n_axes, int32_t keep_dims, fb_tensor* output,
+                 void* stream);
+
+/* Row argmax: index (u32) of the largest element along `axis`, ordered by
+ * the IEEE total order (-0 < +0), lowest index on ties.  No trait method in
+ * the reference; the rule is Tensor::topk's (tensor-core/src/host_tensor/
+ * similarity.rs:82).  Output shape = input with `axis` removed (or kept as
+ * 1).  An empty contraction with a nonempty output is FB_ERR_EMPTY_REDUCTION. */
+int fb_argmax(const fb_tensor* input, uint32_t axis, int32_t keep_dims,
+              fb_tensor* output, void* stream);
+
+/* Sum of every element of an f32 tensor into one f64 on the device
+ * (`partial` is a device pointer to one double).  This is the per-shard
+ * partial of the global sum; callers combine shards with one all-reduce and
+ * finish with fb_finish_sum_f64.  Replaces the multi-pass reduce_all path of
+ * compute-cuda/src/reduction.rs:145-160. */
+int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream);
+
+/* Rounds the device f64 at `partial` into the f32 tensor `output` (one
+ * element, any rank with numel 1). */
+int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream);
+
+/* ------------------------------------------------------------- statistics */
+
+/* TensorStatsBackend (tensor-core/src/statistics.rs:100-129; replaces
+ * compute-cuda/src/statistics.rs:45-252).  Inputs are F32, or F16/BF16 for
+ * the *_low_f32 trait methods (tensor-core/src/low_statistics.rs:25-57),
+ * selected by the input dtype; outputs are always f32. */
+int fb_softmax(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes,
+               fb_tensor* output, void* stream);
+int fb_log_softmax(const fb_tensor* input, const uint32_t* axes,
+                   uint32_t n_axes, fb_tensor* output, void* stream);
+int fb_logsumexp(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes,
+                 int32_t keep_dims, fb_tensor* output, void* stream);
+int fb_moments(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes,
+               int32_t keep_dims, fb_tensor* mean, fb_tensor* variance,
+               void* stream);
+int fb_layer_norm(const fb_tensor* input, const uint32_t* axes,
+                  uint32_t n_axes, float epsilon, fb_tensor* output,
+                  void* stream);
+
+/* ----------------------------------------------------------- low storage */
+
+/* TensorLowBackend::cast_to_low (tensor-core/src/low_precision.rs:310-355;
+ * encode_low at compute-cuda/src/low_precision.cu:6-16): nearest-even f32 ->
+ * F16/BF16 of `output->dtype`; `output` must be contiguous. */
+int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORMA_B200_H */
