@@ -59,12 +59,15 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, bus_id: str | None):
+    def __init__(self, bus_id: str | None, enabled: bool = True):
         self.bus_id = (bus_id or "").lower()
         self.proc = None
         self.file = None
+        self.enabled = enabled
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -72,6 +75,34 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
+
+    @staticmethod
+    def fallback_index() -> str:
+        """nvidia-smi index of this process's GPU when the bus id is unknown."""
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if ids and local < len(ids) and ids[local].isdigit():
+            return ids[local]
+        return str(local)
+
+    def lines(self) -> int:
+        if self.file is None:
+            return 0
+        self.file.flush()
+        try:
+            return len(Path(self.file.name).read_text().splitlines())
+        except OSError:
+            return 0
+
+    def wait_samples(self, keep_busy, count: int, limit_s: float = 5.0) -> None:
+        """Keeps the GPU under the same load until the sampler has written
+        `count` more lines (nvidia-smi needs a few hundred ms to start)."""
+        if self.proc is None:
+            return
+        start, t0 = self.lines(), time.time()
+        while self.lines() < start + count and time.time() - t0 < limit_s:
+            keep_busy()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -93,6 +124,8 @@ class ClockSampler:
             bus = parts[1].lower()
             if self.bus_id and not (bus.endswith(self.bus_id[-12:]) or self.bus_id.endswith(bus[-12:])):
                 continue
+            if not self.bus_id and parts[0] != self.fallback_index():
+                continue
             rows.append(parts)
         os.unlink(self.file.name)
         if not rows:
@@ -107,6 +140,22 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def pci_bus_id(torch, dev) -> str | None:
+    """nvidia-smi style bus id (DDDDDDDD:BB:DD.F) of a torch device, if known."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = getattr(p, "pci_bus_id", None)
+        if isinstance(bus, str):
+            return bus
+        dom = getattr(p, "pci_domain_id", None)
+        dv = getattr(p, "pci_device_id", None)
+        if isinstance(bus, int) and isinstance(dom, int) and isinstance(dv, int):
+            return f"{dom:08X}:{bus:02X}:{dv:02X}.0"
+    except Exception:
+        pass
+    return None
 
 
 # ------------------------------------------------------------- distributed
@@ -269,12 +318,21 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     for name, cin, k, pad in (("conv_bf16_3x3_c3a", 256, 3, 1), ("conv_bf16_1x1_c3b", 1024, 1, 0)):
         xn = torch.randn(256, 14, 14, cin, device=dev, generator=g).bfloat16()
         wn = (torch.randn(256, k, k, cin, device=dev, generator=g) * math.sqrt(2 / (cin * k * k))).bfloat16()
-        xv, wv = xn.permute(0, 3, 1, 2), wn.permute(0, 3, 1, 2)
-        out = torch.empty(256, 14, 14, 256, device=dev).permute(0, 3, 1, 2)  # NHWC f32 storage, NCHW view
+        xv, wv = xn.permute(0, 3, 1, 2), wn.permute(0, 3, 1, 2)  # NHWC / OHWI storage, logical NCHW / OIHW
+        out = torch.empty(256, 256, 14, 14, device=dev)  # contiguous f32 [N, O, P, Q], as the reference allocates
         oc = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
         record(name, lambda: api.conv_low_f32_into(xv, wv, oc, out), 2 * 256 * 14 * 14 * 256 * cin * k * k,
                pk["bf16_tflops"], "measured bf16 dense (burst)")
         del xn, wn, out
+    # C4: causal attention bf16 [8, 32, 4096, 128], scale 1/sqrt(128), f32 output
+    q = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
+    k = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
+    v = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
+    L = 4096
+    record("attention_bf16_causal_c4", lambda: api.attention_low_f32(q, k, v, None, AttentionOptions(causal=0)),
+           4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
+           "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2")
+    del q, k, v
     return res
 
 
@@ -290,8 +348,9 @@ def run_forma(args) -> int:
     dev = torch.device("cuda", dist.local)
     pk = peaks()
     g = torch.Generator(device=dev).manual_seed(1 + dist.rank)
-    x = torch.randn(ROWS, COLS, device=dev, generator=g, dtype=torch.float32)
-    bytes_per = row_bytes(ROWS, COLS)
+    rows = args.rows
+    x = torch.randn(rows, COLS, device=dev, generator=g, dtype=torch.float32)
+    bytes_per = row_bytes(rows, COLS)
     step_bytes = sum(bytes_per.values())
     stream = torch.cuda.current_stream(dev)
 
@@ -304,23 +363,25 @@ def run_forma(args) -> int:
               for k in bytes_per}
     per_kernel_ms = {k: 0.0 for k in bytes_per}
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    bus = None
-    try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
-    except Exception:
-        bus = None
-    launches0 = api.launch_count()
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(bus if isinstance(bus, str) else None) as clocks:
+    def busy():
+        row_ops(api, x, dist)
+        torch.cuda.synchronize(dev)
+
+    with ClockSampler(None if args.no_clocks else pci_bus_id(torch, dev), enabled=not args.no_clocks) as clocks:
+        # Clocks are sampled under the same load just before, during and just
+        # after the timed region (nvidia-smi samples every 200 ms).
+        clocks.wait_samples(busy, 2)
+        launches0 = api.launch_count()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
         start.record(stream)
         for i in range(args.steps):
             step_timers = {k: v[i] for k, v in timers.items()}
             row_ops(api, x, dist, step_timers)
         stop.record(stream)
         torch.cuda.synchronize(dev)
-    dist.barrier()
-    launches = api.launch_count() - launches0
+        launches = api.launch_count() - launches0
+        clocks.wait_samples(busy, 1)
     local_ms = start.elapsed_time(stop)
     for k, evs in timers.items():
         per_kernel_ms[k] = sum(a.elapsed_time(b) for a, b in evs) / args.steps
@@ -335,6 +396,23 @@ def run_forma(args) -> int:
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
 
     # end to end: pinned host input copied in, results read back, every step
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(api, torch, x, dist, dev, stream, step_bytes, args)
+
+    ops = {}
+    if not args.no_ops:
+        ops = run_ops(api, dev, dist, args, pk)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_rows(args.cpu_rows)
+    return emit(args, dist, pk, value, total_ms, step_bytes, dom, achieved, traffic, per_kernel_ms, bytes_per, e2e,
+                launches, clocks, cpu, ops, rows)
+
+
+def run_e2e(api, torch, x, dist, dev, stream, step_bytes, args):
+    ROWS = x.shape[0]
     host_x = torch.empty(ROWS, COLS, dtype=torch.float32, pin_memory=True)
     host_x.copy_(x.cpu())
     outs_host = {k: torch.empty(ROWS, dtype=torch.float32, pin_memory=True) for k in ("row_sum", "row_max", "mean", "var")}
@@ -366,15 +444,12 @@ def run_forma(args) -> int:
     e2e_value = dist.sum(step_bytes * e2e_steps) / (e2e_ms / 1e3) / 1e9
     h2d = ROWS * COLS * 4
     d2h = ROWS * 4 * 5 + 4
+    return {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": e2e_steps}
 
-    ops = {}
-    if not args.no_ops:
-        ops = run_ops(api, dev, dist, args, pk)
 
-    cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        cpu = cpu_baseline_rows(args.cpu_rows)
-
+def emit(args, dist, pk, value, total_ms, step_bytes, dom, achieved, traffic, per_kernel_ms, bytes_per, e2e, launches,
+         clocks, cpu, ops, rows) -> int:
     if dist.rank == 0:
         line = {
             "metric": METRIC,
@@ -391,7 +466,7 @@ def run_forma(args) -> int:
             "data": "synthetic",
             "config": {"workload": "row reductions: X [65536, 4096] f32 ~N(0,1) per GPU; per-row sum, max, argmax, "
                                    "softmax, layer-norm moments; global sum over all ranks (one f64 all-reduce)",
-                       "rows_per_gpu": ROWS, "cols": COLS, "parallelism": f"rows sharded over {dist.world} GPU(s)",
+                       "rows_per_gpu": rows, "cols": COLS, "parallelism": f"rows sharded over {dist.world} GPU(s)",
                        "l2": "inputs larger than L2 (1.07 GB per pass), no flush",
                        "bytes_per_step_per_gpu": step_bytes},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
@@ -400,8 +475,7 @@ def run_forma(args) -> int:
             "kernels_ms": {k: round(v, 4) for k, v in per_kernel_ms.items()},
             "kernels_frac_of_hbm": {k: round(bytes_per[k] / (v / 1e3) / 1e9 / pk["hbm_gbs"], 4)
                                     for k, v in per_kernel_ms.items()},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps},
+            "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
@@ -476,6 +550,9 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-ops", action="store_true", help="skip the conv/attention workloads")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-clocks", action="store_true", help="skip clock sampling (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end pass (profiling runs)")
+    ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "forma":
         args.warmup = 3

@@ -84,6 +84,7 @@ SIGNATURES = {
     "fb_status_string": (C.c_char_p, [C.c_int]),
     "fb_last_error": (C.c_char_p, []),
     "fb_launch_count": (C.c_uint64, []),
+    "fb_device_status": (C.c_uint32, []),
     "fb_conv_plan": (C.c_int, [U64P, C.c_uint32, U64P, C.c_uint32, C.POINTER(FbConvOptions), U64P, U32P]),
     "fb_conv": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
     "fb_conv_low_f32": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),

@@ -397,6 +397,11 @@ def cast_to_low(input: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return out
 
 
+def device_status() -> int:
+    """Synchronises and returns (and clears) the mask of timed-out bounded waits."""
+    return int(lib().fb_device_status())
+
+
 def launch_count() -> int:
     """Kernel launches this library has enqueued."""
     return int(lib().fb_launch_count())

@@ -13,6 +13,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "host.h"
@@ -30,7 +31,7 @@ struct ScratchBlock {
     uint64_t bytes = 0;
 };
 std::mutex g_scratch_mutex;
-std::map<std::pair<int, void*>, ScratchBlock> g_scratch;
+std::map<std::tuple<int, void*, int>, ScratchBlock> g_scratch;
 
 #define FB_TRY(expr)                                          \
     do {                                                      \
@@ -263,7 +264,7 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
     float* result = nullptr;
     View res = out;
     if (round_low) {
-        result = static_cast<float*>(scratch(stream, out.count * 4 + 256));
+        result = static_cast<float*>(scratch(stream, out.count * 4 + 256, SCRATCH_CONV_RESULT));
         if (!result) return fail(FB_ERR_DRIVER, "scratch allocation failed");
         res.data = result;
         res.offset = 0;
@@ -450,11 +451,11 @@ int sm_count() {
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
-void* scratch(void* stream, uint64_t bytes) {
+void* scratch(void* stream, uint64_t bytes, int slot) {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    ScratchBlock& b = g_scratch[{dev, stream}];
+    ScratchBlock& b = g_scratch[std::make_tuple(dev, stream, slot)];
     if (b.bytes >= bytes) return b.ptr;
     // Growing: the old block may still be read by enqueued work on this
     // stream, so it is kept (leaked) rather than freed under the stream.
@@ -502,6 +503,11 @@ const char* fb_status_string(int status) {
 const char* fb_last_error(void) { return last_error_cstr(); }
 
 uint64_t fb_launch_count(void) { return g_launches.load(); }
+
+uint32_t fb_device_status(void) {
+    cudaDeviceSynchronize();
+    return read_reduce_status() | read_gemm_status() | read_attention_status();
+}
 
 int fb_conv_plan(const uint64_t* input_dims, uint32_t input_rank, const uint64_t* weight_dims, uint32_t weight_rank,
                  const fb_conv_options* options, uint64_t* out_dims, uint32_t* out_rank) {

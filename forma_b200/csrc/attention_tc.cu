@@ -1,5 +1,495 @@
-// Placeholder until the tcgen05 flash attention lands.
+// Fused flash attention on the 5th-generation tensor cores (tcgen05).
+//
+// attention_low_f32 for 16-bit Q/K/V, depth D in {64, 128}, no mask tensor,
+// optional causal offset.  One CTA owns 128 query rows of one (batch, head):
+//   warp 0      TMA producer: the Q tile once, then K/V tiles of 128 keys
+//               into a 2-stage shared-memory ring (128B-swizzled boxes of 64
+//               depth columns).
+//   warp 1      TMEM allocator and MMA issuer:
+//                 S_j = Q K_j^T  -> TMEM S buffer j%2 (128 x 128 f32)
+//                 O  += P_j V_j  -> TMEM O (128 x D f32), P from shared memory
+//               S_{j+1} is issued before PV_j so the tensor core computes the
+//               next scores while the softmax warps work on the current ones.
+//   warps 2-5   softmax, one query row per thread: tcgen05.ld of the S row,
+//               scale, causal/length mask, row max, exp2, row sum, P packed
+//               to 16-bit into the swizzled K-major tile; the running max is
+//               only raised (and O rescaled in TMEM) when a row max exceeds it
+//               by more than 2^8, so P <= 2^8 and rescales are rare.
+//               Finally O / l is written as f32.
+// Overflow: BF16 P is stored pre-multiplied by 2^-shift (shift = 9 + log2 of
+// the key count, an exact power of two), so the unnormalised numerator sum P V
+// stays below max|V| and cannot overflow f32 even for V near the format's
+// maximum, which the trait contract requires (tensor-core/src/attention.rs:
+// 41-48); the final O / l divides the same factor out.  F16 needs no shift.
+// Fully masked rows (l == 0) produce zeros.  Every wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "async.cuh"
 #include "kernels.h"
+#include "tc.cuh"
+
 namespace fb {
-int launch_attention_tc(const AttnArgs&, void*) { return FB_ERR_UNSUPPORTED; }
+namespace {
+
+__device__ uint32_t g_attn_status;
+
+constexpr int TQ = 128, TK = 128, THREADS = 192;
+
+struct AttnParams {
+    uint32_t fmt;           // 0 f16, 1 bf16
+    uint32_t L, Lk;         // queries, keys per head
+    uint32_t H, Hkv;        // query heads, key/value heads
+    uint32_t q_tiles, bh;   // query tiles per head, batch x heads
+    uint32_t kv_tiles;
+    float scale_log2;       // scale * log2(e)
+    float shift;            // log2 of the numerator pre-scale
+    int32_t causal, causal_offset;
+    float* out;             // contiguous [..., L, D] f32
+};
+
+template <int D>
+struct ACfg {
+    static constexpr int BOXES = D / 64;               // 64-column swizzle boxes per row
+    static constexpr int Q_BYTES = TQ * D * 2;
+    static constexpr int K_BYTES = TK * D * 2;
+    static constexpr int V_BYTES = TK * D * 2;
+    static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+    static constexpr int STAGES = 2;
+    static constexpr int P_BYTES = TQ * TK * 2;
+    static constexpr int SMEM = 1024 + Q_BYTES + STAGES * STAGE_BYTES + P_BYTES + 256;
+    static constexpr uint32_t S_COL = 0, O_COL = 256, TMEM_COLS = 512;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, uint32_t fmt) {
+    uint32_t r;
+    if (fmt)
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    else
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Shared-memory descriptor of an MN-major, 128B-swizzled operand: 64-element
+// rows along N, 8-row (K) atoms 1024 B apart, N blocks of 64 `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                              const __grid_constant__ CUtensorMap tmK,
+                                                              const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+    using C = ACfg<D>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = smem;
+    unsigned char* sKV = sQ + C::Q_BYTES;
+    unsigned char* sP = sKV + C::STAGES * C::STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+    uint64_t* q_full = bars;           // 1
+    uint64_t* kv_full = bars + 1;      // STAGES
+    uint64_t* kv_empty = bars + 3;     // STAGES
+    uint64_t* s_full = bars + 5;       // 2
+    uint64_t* s_free = bars + 7;       // 2
+    uint64_t* p_full = bars + 9;       // 1
+    uint64_t* pv_done = bars + 10;     // 1
+    uint64_t* drain = bars + 11;       // 1
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Heaviest (last, for causal) query tiles first.
+    const uint32_t bh = blockIdx.x % p.bh;
+    const uint32_t qt = p.q_tiles - 1 - blockIdx.x / p.bh;
+    const uint32_t q0 = qt * TQ;
+    // Key tiles this query tile can see.
+    uint32_t n_kv = p.kv_tiles;
+    if (p.causal) {
+        const int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
+        const int64_t last_key = last_q + (int64_t)p.causal_offset;
+        const int64_t need = last_key < 0 ? 0 : last_key / TK + 1;
+        n_kv = (uint32_t)(need < (int64_t)p.kv_tiles ? need : p.kv_tiles);
+    }
+    const uint32_t batch = bh / p.H, head = bh % p.H;
+    const uint32_t kv_bh = batch * p.Hkv + head / (p.H / p.Hkv);
+    const int32_t q_row0 = (int32_t)(bh * p.L + q0);
+    const int32_t kv_row0 = (int32_t)(kv_bh * p.Lk);
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_free[b], 128);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer
+        if (n_kv > 0) {
+            mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+            for (int b = 0; b < C::BOXES; ++b) tma_load_2d(sQ + b * (TQ * 128), &tmQ, b * 64, q_row0, q_full);
+        }
+        uint32_t issued = 0;
+        bool failed = false;
+        for (uint32_t j = 0; j < n_kv; ++j) {
+            const uint32_t s = j % C::STAGES;
+            if (!mbar_wait(&kv_empty[s], ((j / C::STAGES) & 1) ^ 1)) {
+                failed = true;
+                break;
+            }
+            unsigned char* kd = sKV + s * C::STAGE_BYTES;
+            unsigned char* vd = kd + C::K_BYTES;
+            mbar_arrive_expect_tx(&kv_full[s], C::STAGE_BYTES);
+            for (int b = 0; b < C::BOXES; ++b) {
+                tma_load_2d(kd + b * (TK * 128), &tmK, b * 64, kv_row0 + (int32_t)(j * TK), &kv_full[s]);
+                tma_load_2d(vd + b * (TK * 128), &tmV, b * 64, kv_row0 + (int32_t)(j * TK), &kv_full[s]);
+            }
+            ++issued;
+        }
+        if (failed) {
+            atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+            for (uint32_t j = issued >= C::STAGES ? issued - C::STAGES : 0; j < issued; ++j)
+                (void)mbar_wait(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+        }
+        if (n_kv > 0) (void)mbar_wait(q_full, 0);
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------ MMA issuer
+        const uint32_t idesc_s = f16_idesc(p.fmt, TQ, TK);
+        const uint32_t idesc_o = f16_idesc(p.fmt, TQ, D) | (1u << 16);  // B (V) is MN-major
+        bool ok = n_kv == 0 || mbar_wait(q_full, 0);
+        const uint32_t q_addr = smem_u32(sQ);
+        const uint32_t p_addr = smem_u32(sP);
+        auto issue_s = [&](uint32_t j) -> bool {
+            const uint32_t s = j % C::STAGES, b = j & 1;
+            if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1)) return false;
+            if (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) / 2) & 1)) return false;
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sKV + s * C::STAGE_BYTES);
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+                const uint32_t off = (uint32_t)((k / 4) * (TQ * 128) + (k % 4) * 32);
+                umma_f16_ss(tmem + C::S_COL + b * TK, sw128_desc(q_addr + off), sw128_desc(k_addr + off), idesc_s, k != 0);
+            }
+            umma_commit(&s_full[b]);
+            return true;
+        };
+        auto issue_pv = [&](uint32_t j) -> bool {
+            const uint32_t s = j % C::STAGES;
+            if (!mbar_wait(p_full, j & 1)) return false;
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sKV + s * C::STAGE_BYTES + C::K_BYTES);
+#pragma unroll
+            for (int k = 0; k < TK / 16; ++k) {
+                const uint32_t poff = (uint32_t)((k / 4) * (TQ * 128) + (k % 4) * 32);
+                umma_f16_ss(tmem + C::O_COL, sw128_desc(p_addr + poff), sw128_mn_desc(v_addr + k * 16 * 128, TK * 128),
+                            idesc_o, (j | k) != 0);
+            }
+            umma_commit(pv_done);
+            umma_commit(&kv_empty[s]);
+            return true;
+        };
+        if (ok && n_kv > 0) ok = issue_s(0);
+        for (uint32_t j = 0; ok && j < n_kv; ++j) {
+            if (j + 1 < n_kv) ok = issue_s(j + 1);
+            if (ok) ok = issue_pv(j);
+        }
+        if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ softmax / epilogue
+        const int quarter = warp & 3;
+        const uint32_t row = (uint32_t)(quarter * 32 + lane);
+        const uint32_t q = q0 + row;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        const int64_t vis = p.causal ? (int64_t)q + (int64_t)p.causal_offset : (int64_t)1 << 40;
+        float m_used = -__int_as_float(0x7f800000);  // running max (log2 units)
+        float l = 0.0f;
+        bool ok = true;
+        unsigned char* prow = sP + row * 128;
+        const uint32_t sw = row & 7;
+        for (uint32_t j = 0; j < n_kv && ok; ++j) {
+            const uint32_t b = j & 1;
+            // Wait outcomes are made warp-uniform: tcgen05.ld/st are .sync.aligned.
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j / 2) & 1))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float x[TK];
+            {
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < TK / 32; ++c) {
+                    tmem_ld32(tmem + lane_base + C::S_COL + b * TK + c * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&s_free[b]);
+            // scale into log2 units and mask keys beyond the length / causal edge
+            const int64_t key0 = (int64_t)j * TK;
+            float mt = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int i = 0; i < TK; ++i) {
+                const int64_t key = key0 + i;
+                const bool visible = key < (int64_t)p.Lk && key <= vis;
+                x[i] = visible ? x[i] * p.scale_log2 : -__int_as_float(0x7f800000);
+                mt = fmaxf(mt, x[i]);
+            }
+            float alpha = 1.0f;
+            bool rescale = false;
+            if (mt > m_used + 8.0f) {
+                alpha = m_used == -__int_as_float(0x7f800000) ? 0.0f : ex2(m_used - mt);
+                rescale = j > 0 && l > 0.0f;
+                m_used = mt;
+            }
+            // PV_{j-1} must be done before P is overwritten or O rescaled.
+            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (rescale) {
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_base + C::O_COL + c * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st32(tmem + lane_base + C::O_COL + c * 32, r);
+                }
+                tmem_wait_st();
+            }
+            const float base = m_used == -__int_as_float(0x7f800000) ? 0.0f : m_used + p.shift;
+            float ls = 0.0f;
+#pragma unroll
+            for (int c = 0; c < TK / 8; ++c) {
+                float e[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    e[i] = ex2(x[c * 8 + i] - base);
+                    ls += e[i];
+                }
+                uint4 v;
+                v.x = pack2(e[0], e[1], p.fmt);
+                v.y = pack2(e[2], e[3], p.fmt);
+                v.z = pack2(e[4], e[5], p.fmt);
+                v.w = pack2(e[6], e[7], p.fmt);
+                const uint32_t atom = (uint32_t)(c / 8), chunk = (uint32_t)(c % 8);
+                *reinterpret_cast<uint4*>(prow + atom * (TQ * 128) + ((chunk ^ sw) << 4)) = v;
+            }
+            l = l * alpha + ls;
+            fence_proxy_async_smem();  // P written by generic stores, read by the tensor core
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        // epilogue: O / l, f32 rows
+        if (ok && n_kv > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (n_kv - 1) & 1))) ok = false;
+        if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+        tc_fence_after();
+        // `ok` and n_kv are warp-uniform here, so the loads below are too; only
+        // the stores depend on whether this row exists (q < L).
+        const bool load = ok && n_kv > 0;
+        float* orow = p.out + ((uint64_t)bh * p.L + q) * D;
+        const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            if (load) {
+                tmem_ld32(tmem + lane_base + C::O_COL + c * 32, r);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+            if (q < p.L) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4*>(orow + c * 32 + i) =
+                        make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                    __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_attn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// [rows, D] 16-bit rows, box {64, 128}, 128B swizzle.
+bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t rows, uint64_t D) {
+    auto enc = encode_tiled_attn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {D, rows};
+    cuuint64_t strides[1] = {D * 2};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Rows of a [..., heads, L, D] operand are dense when every row-nest stride
+// equals D times the product of the inner row dims (heads use `heads`).
+bool dense_rows(const AttnArgs& a, const uint64_t* strides, uint64_t heads, uint64_t L, uint64_t D, bool kv) {
+    const int r = (int)a.row_rank;
+    // queries axis
+    if (!kv && strides[r - 1] != D) return false;
+    uint64_t expect = L * D;
+    if (strides[r - 2] != expect && heads > 1) return false;
+    expect *= heads;
+    for (int i = r - 3; i >= 0; --i) {
+        if (a.row_dims[i] > 1 && strides[i] != expect) return false;
+        expect *= a.row_dims[i];
+    }
+    return true;
+}
+
+template <int D>
+int launch_d(const AttnArgs& a, uint32_t fmt, cudaStream_t st) {
+    using C = ACfg<D>;
+    const int r = (int)a.row_rank;
+    const uint64_t L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
+    const uint64_t BH = a.rows / L;
+    const uint64_t B = BH / H;
+    const uint64_t Hkv = H / a.group_size;
+    CUtensorMap tq, tk, tv;
+    const void* q = static_cast<const uint16_t*>(a.q) + a.q_offset;
+    const void* k = static_cast<const uint16_t*>(a.k) + a.k_offset;
+    const void* v = static_cast<const uint16_t*>(a.v) + a.v_offset;
+    if (!make_rows_map(&tq, q, fmt, BH * L, D) || !make_rows_map(&tk, k, fmt, B * Hkv * Lk, D) ||
+        !make_rows_map(&tv, v, fmt, B * Hkv * Lk, D))
+        return FB_ERR_UNSUPPORTED;
+    AttnParams p{};
+    p.fmt = fmt;
+    p.L = (uint32_t)L;
+    p.Lk = (uint32_t)Lk;
+    p.H = (uint32_t)H;
+    p.Hkv = (uint32_t)Hkv;
+    p.q_tiles = (uint32_t)((L + TQ - 1) / TQ);
+    p.bh = (uint32_t)BH;
+    p.kv_tiles = (uint32_t)((Lk + TK - 1) / TK);
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    // P pre-scale for BF16: 2^-(9 + ceil(log2(keys))) keeps sum(P) * max|V|
+    // below max|V| (BF16 shares f32's exponent range, so P stays normal).
+    // F16 values are bounded by 65504 and the numerator cannot approach the
+    // f32 range, while a pre-scale would push P into F16 subnormals: none.
+    p.shift = fmt ? 9.0f + std::ceil(std::log2((float)std::max<uint64_t>(Lk, 1))) : 0.0f;
+    p.causal = a.causal ? 1 : 0;
+    p.causal_offset = a.causal_offset;
+    p.out = a.out + a.o_offset;
+    auto kernel = attn_fwd_kernel<D>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        return FB_ERR_DRIVER;
+    const uint64_t grid = (uint64_t)p.q_tiles * BH;
+    if (grid == 0) return FB_OK;
+    if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
+    kernel<<<(unsigned)grid, THREADS, C::SMEM, st>>>(tq, tk, tv, p);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+}
+
+}  // namespace
+
+uint32_t read_attention_status() {
+    uint32_t v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_attn_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(zero));
+    return v;
+}
+
+int launch_attention_tc(const AttnArgs& a, void* stream) {
+    if (a.dtype != FB_BF16 && a.dtype != FB_F16) return FB_ERR_UNSUPPORTED;
+    if (a.mask_kind != FB_MASK_NONE) return FB_ERR_UNSUPPORTED;
+    if (a.depth != a.value_depth || (a.depth != 64 && a.depth != 128)) return FB_ERR_UNSUPPORTED;
+    if (a.row_rank < 2 || a.keys == 0 || a.rows == 0) return FB_ERR_UNSUPPORTED;
+    const int r = (int)a.row_rank;
+    const uint64_t D = a.depth, L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
+    if (a.q_stride_d != 1 || a.k_stride_d != 1 || a.v_stride_d != 1 || a.o_stride_d != 1) return FB_ERR_UNSUPPORTED;
+    if (a.k_stride_key != D || a.v_stride_key != D) return FB_ERR_UNSUPPORTED;
+    if (H % a.group_size != 0) return FB_ERR_UNSUPPORTED;
+    const uint64_t Hkv = H / a.group_size;
+    if (!dense_rows(a, a.q_row_strides, H, L, D, false) || !dense_rows(a, a.o_row_strides, H, L, D, false) ||
+        !dense_rows(a, a.k_row_strides, Hkv, Lk, D, true) || !dense_rows(a, a.v_row_strides, Hkv, Lk, D, true))
+        return FB_ERR_UNSUPPORTED;
+    // 16-byte aligned operand bases (TMA) and 16-byte aligned output rows.
+    auto aligned = [](const void* p, uint64_t off, uint64_t esz) {
+        return (reinterpret_cast<uintptr_t>(p) + off * esz) % 16 == 0;
+    };
+    if (!aligned(a.q, a.q_offset, 2) || !aligned(a.k, a.k_offset, 2) || !aligned(a.v, a.v_offset, 2) ||
+        !aligned(a.out, a.o_offset, 4))
+        return FB_ERR_UNSUPPORTED;
+    if (a.rows / L * L != a.rows || a.rows * D > (1ull << 40) || L > (1u << 30) || Lk > (1u << 30))
+        return FB_ERR_UNSUPPORTED;
+    const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return D == 64 ? launch_d<64>(a, fmt, st) : launch_d<128>(a, fmt, st);
+}
+
 }  // namespace fb

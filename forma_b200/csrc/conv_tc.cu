@@ -1,5 +1,423 @@
-// Placeholder until the tcgen05 implicit-GEMM convolution lands.
+// Implicit-GEMM convolution on the 5th-generation tensor cores (tcgen05).
+//
+// conv_low_f32 with 16-bit operands is the GEMM
+//     D[m, o] = sum_k A[m, k] * B[o, k]
+// over m = (n, p, q) output pixels, o = output channels and k = (r, s, c)
+// filter taps x input channels, accumulated in f32.
+//   A  channels-last input.  A TMA im2col load gathers 128 output pixels x 64
+//      channels of one tap straight from the NHWC tensor, padding with zeros
+//      at image borders, into a 128B-swizzled K-major shared tile; 1x1
+//      stride-1 convolutions use a plain 2-D [pixels, channels] tiled map.
+//   B  weights as [O, R*S*C] (OHWI storage), 2-D tiled TMA.
+//   D  128 x BN f32 accumulator in TMEM, double-buffered so the epilogue of
+//      one tile overlaps the main loop of the next.
+// Warp roles in a 192-thread CTA, persistent over output tiles:
+//   warp 0      TMA producer (one lane) into a STAGES-deep smem ring
+//   warp 1      TMEM allocator and MMA issuer (one lane)
+//   warps 2-5   epilogue: tcgen05.ld -> f32 stores at the output's strides
+// Every wait is bounded (async.cuh); a timeout sets a status bit and the CTA
+// drains its copies and MMAs before releasing TMEM and exiting.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "async.cuh"
 #include "kernels.h"
+#include "tc.cuh"
+
 namespace fb {
-int launch_conv_tc(const ConvArgs&, void*) { return FB_ERR_UNSUPPORTED; }
+namespace {
+
+__device__ uint32_t g_gemm_status;
+
+constexpr int BM = 128, BK = 64;
+constexpr int THREADS = 192;
+
+struct ConvGemmParams {
+    uint32_t mode;  // 0: A = 2-D [M, C] map, 1: A = im2col map
+    uint32_t fmt;   // 0 f16, 1 bf16
+    uint32_t M, P, Q;
+    uint32_t k_blocks, c_blocks, S;
+    int32_t pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
+    uint32_t m_tiles, n_tiles;
+    float* out;
+    uint64_t out_offset, s_n, s_c, s_p, s_q;
+};
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;  // align slack + ring + barriers
+};
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                               const __grid_constant__ CUtensorMap tmB,
+                                                               ConvGemmParams p) {
+    using C = Cfg<BN>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* ring = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* full = bars;                     // [STAGES]
+    uint64_t* empty = bars + C::STAGES;        // [STAGES]
+    uint64_t* tfull = bars + 2 * C::STAGES;    // [2]
+    uint64_t* tempty = tfull + 2;              // [2]
+    uint64_t* drain = tempty + 2;              // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tiles = p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4 * 32);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer
+        uint32_t stage = 0, phase = 0;
+        uint64_t issued = 0;
+        bool failed = false;
+        for (uint32_t t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+            const uint32_t mt = t / p.n_tiles, nt = t % p.n_tiles;
+            const uint32_t m0 = mt * BM;
+            const uint32_t pq = p.P * p.Q;
+            const int32_t n0 = (int32_t)(m0 / pq), rem = (int32_t)(m0 % pq);
+            const int32_t w0 = (rem % (int32_t)p.Q) * p.stride_w - p.pad_w;
+            const int32_t h0 = (rem / (int32_t)p.Q) * p.stride_h - p.pad_h;
+            for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1)) {
+                    atomicOr(&g_gemm_status, 1u << DEV_GEMM_PRODUCER_TIMEOUT);
+                    failed = true;
+                    break;
+                }
+                unsigned char* a_dst = ring + stage * C::STAGE_BYTES;
+                unsigned char* b_dst = a_dst + C::A_BYTES;
+                mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                const uint32_t cb = kb % p.c_blocks, tap = kb / p.c_blocks;
+                if (p.mode == 0) {
+                    tma_load_2d(a_dst, &tmA, (int32_t)(cb * BK), (int32_t)m0, &full[stage]);
+                } else {
+                    const uint32_t r = tap / p.S, s = tap % p.S;
+                    tma_load_im2col_4d(a_dst, &tmA, (int32_t)(cb * BK), w0, h0, n0, (uint16_t)(s * p.dil_w),
+                                       (uint16_t)(r * p.dil_h), &full[stage]);
+                }
+                tma_load_2d(b_dst, &tmB, (int32_t)(kb * BK), (int32_t)(nt * BN), &full[stage]);
+                ++issued;
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        if (failed) {
+            // Let the loads already issued land before the CTA can exit.
+            uint32_t s = stage, ph = phase;
+            for (int i = 0; i < C::STAGES && issued > 0; ++i, --issued) {
+                if (s == 0) {
+                    s = C::STAGES;
+                    ph ^= 1;
+                }
+                --s;
+                (void)mbar_wait(&full[s], ph);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------ MMA issuer
+        const uint32_t idesc = f16_idesc(p.fmt, BM, BN);
+        uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+        bool failed = false;
+        for (uint32_t t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+            if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + acc * BN;
+            for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                if (!mbar_wait(&full[stage], phase)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(ring + stage * C::STAGE_BYTES);
+                const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    umma_f16_ss(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+                umma_commit(&empty[stage]);  // frees the stage when these MMAs complete
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (failed) break;
+            umma_commit(&tfull[acc]);  // accumulator complete
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (failed) atomicOr(&g_gemm_status, 1u << DEV_GEMM_MMA_TIMEOUT);
+        // All MMAs issued by this thread have finished once `drain` completes.
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ epilogue
+        const int quarter = warp & 3;  // TMEM lanes [32*quarter, +32)
+        const int row = quarter * 32 + lane;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+            // Warp-uniform outcome: the tcgen05.ld below is .sync.aligned.
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase))) {
+                atomicOr(&g_gemm_status, 1u << DEV_GEMM_EPILOGUE_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t mt = t / p.n_tiles, nt = t % p.n_tiles;
+            const uint32_t m = mt * BM + row;
+            float* base = nullptr;
+            if (m < p.M) {
+                const uint32_t pq = p.P * p.Q;
+                const uint32_t n = m / pq, r = m % pq;
+                base = p.out + p.out_offset + (uint64_t)n * p.s_n + (uint64_t)(r / p.Q) * p.s_p + (uint64_t)(r % p.Q) * p.s_q +
+                       (uint64_t)(nt * BN) * p.s_c;
+            }
+            const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                tmem_wait_ld();
+                if (base) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) base[(uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col() {
+    static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D K-major tile map over rows x cols 16-bit elements (cols contiguous,
+// row pitch `pitch` elements), box {64, box_rows}, 128B swizzle.
+bool make_2d_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t cols, uint64_t rows, uint64_t pitch,
+                 uint32_t box_rows) {
+    auto enc = encode_tiled();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch * 2};
+    cuuint32_t box[2] = {BK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_im2col_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t C, uint64_t W, uint64_t H, uint64_t N,
+                     int lower_w, int lower_h, int upper_w, int upper_h, uint32_t stride_w, uint32_t stride_h) {
+    auto enc = encode_im2col();
+    if (!enc) return false;
+    cuuint64_t dims[4] = {C, W, H, N};
+    cuuint64_t strides[3] = {C * 2, W * C * 2, H * W * C * 2};
+    int lower[2] = {lower_w, lower_h};
+    int upper[2] = {upper_w, upper_h};
+    cuuint32_t estr[4] = {1, stride_w, stride_h, 1};
+    return enc(map, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr),
+               dims, strides, lower, upper, BK, BM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Gathers OIHW-viewed weights into dense [O, R, S, C] rows (K-major B).
+template <typename E>
+__global__ void weights_to_ohwi_kernel(const E* w, uint64_t off, uint64_t so, uint64_t sc, uint64_t sr, uint64_t ss,
+                                       uint32_t O, uint32_t Cc, uint32_t R, uint32_t S, E* out) {
+    const uint64_t total = (uint64_t)O * R * S * Cc;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t c = i % Cc;
+        uint64_t t = i / Cc;
+        const uint32_t s = t % S;
+        t /= S;
+        const uint32_t r = t % R;
+        const uint32_t o = t / R;
+        out[i] = w[off + o * so + c * sc + r * sr + s * ss];
+    }
+}
+
+template <int BN>
+int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams& p, cudaStream_t st) {
+    using C = Cfg<BN>;
+    auto kernel = conv_gemm_kernel<BN>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        return FB_ERR_DRIVER;
+    const uint32_t tiles = p.m_tiles * p.n_tiles;
+    const uint32_t grid = tiles < (uint32_t)sm_count() ? tiles : (uint32_t)sm_count();
+    kernel<<<grid, THREADS, C::SMEM, st>>>(ta, tb, p);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+}
+
+}  // namespace
+
+uint32_t read_gemm_status() {
+    uint32_t v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(zero));
+    return v;
+}
+
+int launch_conv_tc(const ConvArgs& a, void* stream) {
+    if (a.dtype != FB_BF16 && a.dtype != FB_F16) return FB_ERR_UNSUPPORTED;
+    if (a.spatial != 2 || a.outputs_per_group != a.out_channels) return FB_ERR_UNSUPPORTED;  // 2-D, one group
+    const uint64_t C = a.channels_per_group, H = a.in_dims[0], W = a.in_dims[1];
+    const uint64_t R = a.k_dims[0], S = a.k_dims[1], O = a.out_channels;
+    const uint64_t P = a.out_dims[0], Q = a.out_dims[1], N = a.batch;
+    if (C % BK != 0 || O % 16 != 0 || O == 0) return FB_ERR_UNSUPPORTED;
+    // Channels-last input: c stride 1, w stride C, h stride W*C, n stride H*W*C.
+    if (a.in_stride_c != 1 || a.in_strides[1] != C || a.in_strides[0] != W * C || a.in_stride_n != H * W * C)
+        return FB_ERR_UNSUPPORTED;
+    const uintptr_t in_addr = reinterpret_cast<uintptr_t>(a.input) + a.in_offset * 2;
+    if (in_addr % 16 != 0) return FB_ERR_UNSUPPORTED;
+    const uint64_t M = N * P * Q;
+    if (M == 0 || M > 0x7fffffffull || N * H * W * C > (1ull << 40)) return FB_ERR_UNSUPPORTED;
+    const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
+    const bool one_by_one = R == 1 && S == 1 && a.stride[0] == 1 && a.stride[1] == 1 && a.pad[0] == 0 && a.pad[1] == 0 &&
+                            P == H && Q == W;
+    // im2col corners: lower = -pad_before, upper = pad_after - (k - 1) * dilation,
+    // each within [-128, 127] for two spatial dimensions; traversal stride <= 8.
+    const int64_t pa_h = (int64_t)((P - 1) * a.stride[0] + (R - 1) * a.dilation[0] + 1) - (int64_t)(H + a.pad[0]);
+    const int64_t pa_w = (int64_t)((Q - 1) * a.stride[1] + (S - 1) * a.dilation[1] + 1) - (int64_t)(W + a.pad[1]);
+    const int64_t lower_h = -(int64_t)a.pad[0], lower_w = -(int64_t)a.pad[1];
+    const int64_t upper_h = pa_h - (int64_t)((R - 1) * a.dilation[0]);
+    const int64_t upper_w = pa_w - (int64_t)((S - 1) * a.dilation[1]);
+    auto corner_ok = [](int64_t v) { return v >= -128 && v <= 127; };
+    const bool im2col_ok = corner_ok(lower_h) && corner_ok(lower_w) && corner_ok(upper_h) && corner_ok(upper_w) &&
+                           a.stride[0] <= 8 && a.stride[1] <= 8 && (R - 1) * a.dilation[0] < 65536 &&
+                           (S - 1) * a.dilation[1] < 65536 && N * H * W * C * 2 >= (128u << 10);
+    if (!one_by_one && !im2col_ok) return FB_ERR_UNSUPPORTED;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    // B operand: dense [O, R*S*C] rows; gather when the weights are not OHWI.
+    const uint64_t K = R * S * C;
+    const void* wptr = static_cast<const uint16_t*>(a.weight) + a.w_offset;
+    const bool ohwi = a.w_stride_c == 1 && a.w_strides[1] == C && a.w_strides[0] == S * C && a.w_stride_o == K &&
+                      reinterpret_cast<uintptr_t>(wptr) % 16 == 0;
+    if (!ohwi) {
+        void* tmp = scratch(stream, O * K * 2 + 256, SCRATCH_CONV_WEIGHT);
+        if (!tmp) return FB_ERR_DRIVER;
+        const uint64_t total = O * K;
+        const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 8);
+        weights_to_ohwi_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.weight), a.w_offset,
+                                                               a.w_stride_o, a.w_stride_c, a.w_strides[0], a.w_strides[1],
+                                                               (uint32_t)O, (uint32_t)C, (uint32_t)R, (uint32_t)S,
+                                                               static_cast<uint16_t*>(tmp));
+        count_launch();
+        if (cudaGetLastError() != cudaSuccess) return FB_ERR_DRIVER;
+        wptr = tmp;
+    }
+    const int BN = O % 256 == 0 ? 256 : O % 128 == 0 ? 128 : O % 64 == 0 ? 64 : 0;
+    if (BN == 0) return FB_ERR_UNSUPPORTED;
+
+    CUtensorMap ta, tb;
+    const void* in_ptr = static_cast<const uint16_t*>(a.input) + a.in_offset;
+    if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN)) return FB_ERR_UNSUPPORTED;
+    ConvGemmParams p{};
+    if (one_by_one) {
+        if (!make_2d_map(&ta, in_ptr, fmt, C, M, C, BM)) return FB_ERR_UNSUPPORTED;
+        p.mode = 0;
+    } else {
+        if (!make_im2col_map(&ta, in_ptr, fmt, C, W, H, N, (int)lower_w, (int)lower_h, (int)upper_w, (int)upper_h,
+                             (uint32_t)a.stride[1], (uint32_t)a.stride[0]))
+            return FB_ERR_UNSUPPORTED;
+        p.mode = 1;
+    }
+    p.fmt = fmt;
+    p.M = (uint32_t)M;
+    p.P = (uint32_t)P;
+    p.Q = (uint32_t)Q;
+    p.c_blocks = (uint32_t)(C / BK);
+    p.k_blocks = (uint32_t)(K / BK);
+    p.S = (uint32_t)S;
+    p.pad_h = (int32_t)a.pad[0];
+    p.pad_w = (int32_t)a.pad[1];
+    p.stride_h = (int32_t)a.stride[0];
+    p.stride_w = (int32_t)a.stride[1];
+    p.dil_h = (int32_t)a.dilation[0];
+    p.dil_w = (int32_t)a.dilation[1];
+    p.m_tiles = (uint32_t)((M + BM - 1) / BM);
+    p.n_tiles = (uint32_t)(O / BN);
+    p.out = a.output;
+    p.out_offset = a.out_offset;
+    p.s_n = a.out_stride_n;
+    p.s_c = a.out_stride_c;
+    p.s_p = a.out_strides[0];
+    p.s_q = a.out_strides[1];
+    switch (BN) {
+        case 256: return launch_bn<256>(ta, tb, p, st);
+        case 128: return launch_bn<128>(ta, tb, p, st);
+        default: return launch_bn<64>(ta, tb, p, st);
+    }
+}
+
 }  // namespace fb

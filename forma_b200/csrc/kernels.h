@@ -67,11 +67,24 @@ enum StatsOp : uint32_t {
     STATS_MOMENTS = 4,
 };
 
-// Library-owned scratch for the calling (device, stream) pair; grows on
-// demand and lives until process exit.  Returns nullptr on allocation failure.
-void* scratch(void* stream, uint64_t bytes);
+// Library-owned scratch for the calling (device, stream, slot); grows on
+// demand and lives until process exit.  Each slot serves one purpose so that
+// buffers used within one call (or carrying state between calls, like the
+// global sum's re-armed counter) never alias.  Returns nullptr on failure.
+enum ScratchSlot : int {
+    SCRATCH_SUM = 0,          // global-sum block partials + finishing counter
+    SCRATCH_CONV_RESULT = 1,  // f32 convolution result before low rounding
+    SCRATCH_CONV_WEIGHT = 2,  // weights gathered into [O, kh, kw, C]
+    SCRATCH_SLOTS = 3,
+};
+void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
 void count_launch();
+
+// Per translation unit: reads and clears the device status word.
+uint32_t read_reduce_status();
+uint32_t read_gemm_status();
+uint32_t read_attention_status();
 
 // ---- reductions / statistics (reduce.cu) ----
 int launch_reduce_rows(uint32_t op, const Rows& in, const RowOut& out, void* stream);

@@ -14,11 +14,16 @@
 // argmax compare total-order keys so they are exact and order-independent.
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
+#include "async.cuh"
 #include "device_common.cuh"
 #include "kernels.h"
 
 namespace fb {
 namespace {
+
+__device__ uint32_t g_reduce_status;  // DeviceStatus of this translation unit
 
 constexpr int BLOCK = 256;
 
@@ -223,8 +228,10 @@ __global__ void __launch_bounds__(BLOCK) stats_rows_kernel(Rows in, ElemOut out,
                 const double inv = 1.0 / s;
                 emit([&](float x) { return (float)((double)expf(x - m) * inv); });
             } else if (op == STATS_LOG_SOFTMAX) {
-                const double shift = (double)m + log(s);
-                emit([&](float x) { return (float)((double)x - shift); });
+                // (x - max) - log(sum): subtracting the shift first keeps the
+                // result exact for huge offsets (max + log(sum) would round).
+                const double ls = log(s);
+                emit([&](float x) { return (float)(((double)x - (double)m) - ls); });
             } else if (threadIdx.x == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(s));
             }
@@ -246,6 +253,251 @@ __global__ void __launch_bounds__(BLOCK) stats_rows_kernel(Rows in, ElemOut out,
                 static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
             }
         }
+    }
+}
+
+// Streamed row engine for contiguous rows (the row-reduction workload).
+//
+// Rows are copied HBM -> shared memory by cp.async.bulk into a ring of
+// `stages` row buffers, each completing on its own mbarrier, so the next rows
+// are always in flight while the current one is reduced: the block never
+// waits on an HBM round trip between rows.  Each thread then takes NV float4
+// of the row into registers (conflict-free 16-byte shared loads), the stage is
+// released, and the operation runs on registers with block-wide f64 / key
+// reductions.  Elementwise results leave with 128-bit coalesced stores.
+template <typename T>
+__device__ __forceinline__ float4 smem_load4(const unsigned char* row, uint64_t v) {
+    if constexpr (sizeof(T) == 4) {
+        return *reinterpret_cast<const float4*>(row + v * 16);
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(row + v * 8);
+        if constexpr (std::is_same<T, __nv_bfloat16>::value)
+            return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                               __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+        else
+            return make_float4(f16_bits_to_float((uint16_t)(u.x & 0xffff)), f16_bits_to_float((uint16_t)(u.x >> 16)),
+                               f16_bits_to_float((uint16_t)(u.y & 0xffff)), f16_bits_to_float((uint16_t)(u.y >> 16)));
+    }
+}
+
+// Operation codes of the streamed engine: RowOp values, then StatsOp + 16.
+constexpr uint32_t STREAM_STATS = 16;
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
+                                                            float eps, uint32_t stages, uint32_t row_bytes) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    unsigned char* ring = smem + 128;
+    // Per-warp partials, double-buffered by row parity so that one barrier per
+    // block reduction suffices (a row's partials are never overwritten before
+    // every thread has passed the next row's first barrier).
+    __shared__ double s_d[2][2][BLOCK / 32];
+    __shared__ float s_f[2][BLOCK / 32];
+    __shared__ uint64_t s_k[2][BLOCK / 32];
+    __shared__ int s_abort;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint64_t first = blockIdx.x, step = gridDim.x;
+    const uint64_t mine = first < in.rows ? (in.rows - 1 - first) / step + 1 : 0;
+    const uint64_t n = in.cols;
+    const T* base = reinterpret_cast<const T*>(in.data) + in.offset;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    auto issue = [&](uint64_t i) {
+        const uint32_t s = (uint32_t)(i % stages);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[s], row_bytes);
+        bulk_g2s(ring + (uint64_t)s * row_bytes, base + (first + i * step) * in.row_stride, row_bytes, &full[s]);
+    };
+    if (tid == 0)
+        for (uint64_t i = 0; i < mine && i < stages; ++i) issue(i);
+    uint64_t aborted_at = ~0ull;
+    for (uint64_t i = 0; i < mine; ++i) {
+        const uint32_t s = (uint32_t)(i % stages), par = (uint32_t)(i & 1);
+        if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) s_abort = 1;
+        float4 c[NV];
+        const unsigned char* rb = ring + (uint64_t)s * row_bytes;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const uint64_t v = tid + (uint64_t)j * BLOCK;
+            c[j] = v * 4 < n ? smem_load4<T>(rb, v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const uint64_t row = first + i * step;
+        // First barrier of the row: every thread has read stage s, so the
+        // producer refills it, and the first partials are visible.
+        auto barrier_release = [&]() {
+            __syncthreads();
+            if (tid == 0 && i + stages < mine && !s_abort) issue(i + stages);
+        };
+        auto valid = [&](int j) { return (tid + (uint64_t)j * BLOCK) * 4 < n; };
+
+        if (op == ROW_SUM || op == ROW_MEAN) {
+            double a = 0.0;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (valid(j)) a += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
+            a = warp_sum(a);
+            if (lane == 0) s_d[0][par][warp] = a;
+            barrier_release();
+            if (s_abort) {
+                aborted_at = i;
+                break;
+            }
+            if (tid == 0) {
+                double t = 0.0;
+#pragma unroll
+                for (int w = 0; w < BLOCK / 32; ++w) t += s_d[0][par][w];
+                static_cast<float*>(oa.data)[out_index(oa, row)] = op == ROW_MEAN ? (float)(t / (double)n) : (float)t;
+            }
+        } else if (op == ROW_MIN || op == ROW_MAX || op == ROW_ARGMAX) {
+            // Keys in column order per thread: a strictly greater key wins,
+            // so each thread keeps its lowest column among equal keys.
+            const uint32_t flip = op == ROW_MIN ? 0xffffffffu : 0u;
+            uint32_t bk = 0, bc = 0;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) continue;
+                const uint32_t col = (uint32_t)((tid + (uint64_t)j * BLOCK) * 4);
+                const float xs[4] = {c[j].x, c[j].y, c[j].z, c[j].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t k = order_key(xs[e]) ^ flip;
+                    if (k > bk || (j == 0 && e == 0)) {
+                        bk = k;
+                        bc = col + e;
+                    }
+                }
+            }
+            uint64_t best = ((uint64_t)bk << 32) | (uint64_t)(0xffffffffu - bc);
+            if (!valid(0)) best = 0;
+            best = warp_max_u64(best);
+            if (lane == 0) s_k[par][warp] = best;
+            barrier_release();
+            if (s_abort) {
+                aborted_at = i;
+                break;
+            }
+            if (tid == 0) {
+                uint64_t t = s_k[par][0];
+#pragma unroll
+                for (int w = 1; w < BLOCK / 32; ++w) t = s_k[par][w] > t ? s_k[par][w] : t;
+                const uint32_t k = (uint32_t)(t >> 32) ^ flip;
+                if (op == ROW_ARGMAX)
+                    static_cast<uint32_t*>(oa.data)[out_index(oa, row)] = 0xffffffffu - (uint32_t)(t & 0xffffffffu);
+                else
+                    static_cast<float*>(oa.data)[out_index(oa, row)] = key_value(k);
+            }
+        } else if (op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
+                   op == STREAM_STATS + STATS_LOGSUMEXP) {
+            float m = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (valid(j)) m = fmaxf(m, fmaxf(fmaxf(c[j].x, c[j].y), fmaxf(c[j].z, c[j].w)));
+            m = warp_max(m);
+            if (lane == 0) s_f[par][warp] = m;
+            barrier_release();
+            if (s_abort) {
+                aborted_at = i;
+                break;
+            }
+            m = s_f[par][0];
+#pragma unroll
+            for (int w = 1; w < BLOCK / 32; ++w) m = fmaxf(m, s_f[par][w]);
+            // exp(x - max) once per element (kept in registers for softmax);
+            // each thread's terms are summed in f32, threads combine in f64.
+            float e = 0.0f;
+            const bool keep = op == STREAM_STATS + STATS_SOFTMAX;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) continue;
+                const float4 x = c[j];
+                const float4 ex = make_float4(expf(x.x - m), expf(x.y - m), expf(x.z - m), expf(x.w - m));
+                e += (ex.x + ex.y) + (ex.z + ex.w);
+                if (keep) c[j] = ex;
+            }
+            double ed = warp_sum((double)e);
+            if (lane == 0) s_d[1][par][warp] = ed;
+            __syncthreads();
+            ed = 0.0;
+#pragma unroll
+            for (int w = 0; w < BLOCK / 32; ++w) ed += s_d[1][par][w];
+            if (op == STREAM_STATS + STATS_SOFTMAX) {
+                const float inv = (float)(1.0 / ed);
+                float* orow = eo.data + eo.offset + row * eo.row_stride;
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j))
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                            make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv);
+            } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
+                const double ls = log(ed);
+                float* orow = eo.data + eo.offset + row * eo.row_stride;
+                auto lsm = [&](float x) { return (float)(((double)x - (double)m) - ls); };
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j))
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                            make_float4(lsm(c[j].x), lsm(c[j].y), lsm(c[j].z), lsm(c[j].w));
+            } else if (tid == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(ed));
+            }
+        } else {
+            // Moments / layer norm: f64 mean, then f64 centred squares, so any
+            // finite f32 input (up to f32::MAX) keeps a finite normalisation.
+            double a = 0.0;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (valid(j)) a += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
+            a = warp_sum(a);
+            if (lane == 0) s_d[0][par][warp] = a;
+            barrier_release();
+            if (s_abort) {
+                aborted_at = i;
+                break;
+            }
+            a = 0.0;
+#pragma unroll
+            for (int w = 0; w < BLOCK / 32; ++w) a += s_d[0][par][w];
+            const double mean = a / (double)n;
+            double q = 0.0;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) continue;
+                const double d0 = (double)c[j].x - mean, d1 = (double)c[j].y - mean;
+                const double d2 = (double)c[j].z - mean, d3 = (double)c[j].w - mean;
+                q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+            }
+            q = warp_sum(q);
+            if (lane == 0) s_d[1][par][warp] = q;
+            __syncthreads();
+            q = 0.0;
+#pragma unroll
+            for (int w = 0; w < BLOCK / 32; ++w) q += s_d[1][par][w];
+            const double var = q / (double)n;
+            if (op == STREAM_STATS + STATS_LAYER_NORM) {
+                const double inv = 1.0 / sqrt(var + (double)eps);
+                float* orow = eo.data + eo.offset + row * eo.row_stride;
+                auto ln = [&](float x) { return (float)(((double)x - mean) * inv); };
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j))
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                            make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w));
+            } else if (tid == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
+                static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
+            }
+        }
+    }
+    if (aborted_at != ~0ull && tid == 0) {
+        atomicOr(&g_reduce_status, 1u << DEV_ROWS_WAIT_TIMEOUT);
+        // Drain the copies still in flight (bounded) before the block exits.
+        for (uint64_t i = aborted_at; i < mine && i < aborted_at + stages; ++i)
+            (void)mbar_wait(&full[i % stages], (uint32_t)((i / stages) & 1));
     }
 }
 
@@ -372,11 +624,72 @@ int stats_typed(uint32_t op, const Rows& in, const ElemOut& out, const RowOut& a
     return check_launch();
 }
 
+// Launches the streamed engine when the geometry allows it; returns
+// FB_ERR_UNSUPPORTED otherwise.
+template <typename T>
+int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, const ElemOut& eo, float eps,
+                 cudaStream_t st) {
+    const uint64_t esz = sizeof(T);
+    const uint64_t row_bytes = in.cols * esz;
+    if (!in.contiguous_rows || in.cols == 0 || in.cols % 4 != 0 || row_bytes % 16 != 0) return FB_ERR_UNSUPPORTED;
+    if (in.cols > 8ull * 4 * BLOCK) return FB_ERR_UNSUPPORTED;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(in.data) + in.offset * esz;
+    if (addr % 16 != 0 || (in.rows > 1 && (in.row_stride * esz) % 16 != 0)) return FB_ERR_UNSUPPORTED;
+    const bool elementwise = op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
+                             op == STREAM_STATS + STATS_LAYER_NORM;
+    if (elementwise && !(eo.contiguous_rows && reinterpret_cast<uintptr_t>(eo.data + eo.offset) % 16 == 0 &&
+                         (in.rows <= 1 || eo.row_stride % 4 == 0)))
+        return FB_ERR_UNSUPPORTED;
+    const uint64_t vec = in.cols / 4;
+    const int nv = vec <= BLOCK ? 1 : vec <= 2 * BLOCK ? 2 : vec <= 4 * BLOCK ? 4 : 8;
+    // Ring depth: enough rows in flight to cover HBM latency, within shared memory.
+    uint32_t stages = row_bytes <= 4096 ? 8 : row_bytes <= 8192 ? 5 : 3;
+    auto launch = [&](auto kernel) -> int {
+        const size_t smem = 128 + (size_t)stages * row_bytes;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return FB_ERR_DRIVER;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, BLOCK, smem) != cudaSuccess || per_sm < 1)
+            return FB_ERR_UNSUPPORTED;
+        const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
+        const unsigned grid = (unsigned)(in.rows < cap ? in.rows : cap);
+        kernel<<<grid, BLOCK, smem, st>>>(in, op, a, b, eo, eps, stages, (uint32_t)row_bytes);
+        return check_launch();
+    };
+    switch (nv) {
+        case 1: return launch(rows_stream_kernel<T, 1>);
+        case 2: return launch(rows_stream_kernel<T, 2>);
+        case 4: return launch(rows_stream_kernel<T, 4>);
+        default: return launch(rows_stream_kernel<T, 8>);
+    }
+}
+
+int stream_rows(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, const ElemOut& eo, float eps,
+                cudaStream_t st) {
+    switch (in.dtype) {
+        case FB_F32: return stream_typed<float>(op, in, a, b, eo, eps, st);
+        case FB_BF16: return stream_typed<__nv_bfloat16>(op, in, a, b, eo, eps, st);
+        case FB_F16: return stream_typed<__half>(op, in, a, b, eo, eps, st);
+        default: return FB_ERR_UNSUPPORTED;
+    }
+}
+
 }  // namespace
+
+uint32_t read_reduce_status() {
+    uint32_t v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_reduce_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    cudaMemcpyToSymbol(g_reduce_status, &zero, sizeof(zero));
+    return v;
+}
 
 int launch_reduce_rows(uint32_t op, const Rows& in, const RowOut& out, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (in.rows == 0) return FB_OK;
+    if (op != ROW_PRODUCT && in.dtype != FB_U32) {
+        const int r = stream_rows(op, in, out, RowOut{}, ElemOut{}, 0.0f, s);
+        if (r != FB_ERR_UNSUPPORTED) return r;
+    }
     switch (in.dtype) {
         case FB_F32: return reduce_typed<float>(op, in, out, s);
         case FB_BF16: return reduce_typed<__nv_bfloat16>(op, in, out, s);
@@ -392,6 +705,8 @@ int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const Row
                       void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (in.rows == 0) return FB_OK;
+    const int r = stream_rows(STREAM_STATS + op, in, a, b, out, eps, s);
+    if (r != FB_ERR_UNSUPPORTED) return r;
     switch (in.dtype) {
         case FB_F32: return stats_typed<float>(op, in, out, a, b, eps, s);
         case FB_BF16: return stats_typed<__nv_bfloat16>(op, in, out, a, b, eps, s);
@@ -404,7 +719,7 @@ int launch_sum_partial(const Rows& in, double* partial, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned g = (unsigned)sm_count() * 4;
     // Scratch layout: [g doubles of block partials][one u32 counter].
-    char* scr = static_cast<char*>(scratch(stream, (uint64_t)g * sizeof(double) + 256));
+    char* scr = static_cast<char*>(scratch(stream, (uint64_t)g * sizeof(double) + 256, SCRATCH_SUM));
     if (!scr) return FB_ERR_DRIVER;
     double* partials = reinterpret_cast<double*>(scr);
     unsigned* counter = reinterpret_cast<unsigned*>(scr + (uint64_t)g * sizeof(double));

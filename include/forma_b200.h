@@ -127,6 +127,11 @@ const char* fb_status_string(int status);
 const char* fb_last_error(void);
 /* Number of kernel launches this library has enqueued (all threads). */
 uint64_t fb_launch_count(void);
+/* Synchronises the current device and returns (and clears) a bit mask of
+ * bounded waits that timed out inside this library's kernels since the last
+ * call (0 = none).  A kernel that gives up a wait writes no partial result
+ * beyond what it had finished and releases its resources. */
+uint32_t fb_device_status(void);
 
 /* ------------------------------------------------------------ convolution */
 
@@ -234,6 +239,7 @@ int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream);
 /* Rounds the device f64 at `partial` into the f32 tensor `output` (one
  * element, any rank with numel 1). */
 int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream);
+
 
 /* ------------------------------------------------------------- statistics */
 

@@ -1,0 +1,79 @@
+"""The tcgen05 flash-attention path versus the f64 oracle.  Shapes are dense
+[B, H, L, D] with D in {64, 128} and no mask tensor, which route to the
+tensor-core kernel."""
+
+import numpy as np
+import pytest
+import torch
+
+from forma_b200 import api
+from forma_b200.api import AttentionOptions
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def check(cuda, qs, ks, vs, causal=None, scale=None, dtype=torch.bfloat16, seed=0, vconst=None):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(*qs, generator=g).to(dtype)
+    k = torch.randn(*ks, generator=g).to(dtype)
+    v = torch.randn(*vs, generator=g).to(dtype) if vconst is None else torch.full(vs, vconst).to(dtype)
+    before = api.launch_count()
+    out = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), None, AttentionOptions(scale, causal)).cpu().numpy()
+    assert api.device_status() == 0, "a bounded wait timed out"
+    assert api.launch_count() > before
+    ref = orc.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), None, scale, causal,
+                        nthreads=orc.threads())
+    assert out.shape == ref.shape
+    assert np.isfinite(out).all()
+    scale_e = max(float(np.abs(ref).max()), 1e-30)
+    err = float(np.abs(out.astype(np.float64) - ref).max()) / scale_e
+    assert err <= 2e-2, err  # parity gate for bf16 tensor-core ops
+    assert err <= 5e-3, err  # the kernel's own accuracy (bf16 P, f32 accumulate)
+    return out, ref
+
+
+def test_tc_attention_causal_d128(cuda):
+    check(cuda, (1, 2, 256, 128), (1, 2, 256, 128), (1, 2, 256, 128), causal=0)
+
+
+def test_tc_attention_ragged_noncausal_d128(cuda):
+    check(cuda, (1, 2, 300, 128), (1, 2, 300, 128), (1, 2, 300, 128))
+
+
+def test_tc_attention_vit_shape_d64(cuda):
+    check(cuda, (2, 3, 197, 64), (2, 3, 197, 64), (2, 3, 197, 64))
+
+
+def test_tc_attention_gqa_and_offsets(cuda):
+    for causal in (-5, 100, -300):
+        out, ref = check(cuda, (1, 4, 256, 64), (1, 2, 256, 64), (1, 2, 256, 64), causal=causal, seed=7)
+        if causal == -300:
+            assert (out == 0).all()  # every row fully masked
+
+
+def test_tc_attention_f16_and_scale(cuda):
+    check(cuda, (1, 2, 256, 128), (1, 2, 384, 128), (1, 2, 384, 128), causal=128, scale=0.05, dtype=torch.float16)
+
+
+def test_tc_attention_large_values_do_not_overflow(cuda):
+    big = 3.3e38  # near the bf16 maximum: the unnormalised numerator must stay finite
+    out, ref = check(cuda, (1, 1, 128, 64), (1, 1, 4096, 64), (1, 1, 4096, 64), vconst=big)
+    assert np.isfinite(out).all()
+
+
+def test_tc_attention_c4_size_sampled(cuda):
+    """Causal attention at the workload size [8, 32, 4096, 128]: the full
+    tensor is computed, two (batch, head) pairs are compared to the oracle."""
+    g = torch.Generator(device=cuda).manual_seed(2)
+    q = torch.randn(8, 32, 4096, 128, device=cuda, generator=g).bfloat16()
+    k = torch.randn(8, 32, 4096, 128, device=cuda, generator=g).bfloat16()
+    v = torch.randn(8, 32, 4096, 128, device=cuda, generator=g).bfloat16()
+    out = api.attention_low_f32(q, k, v, None, AttentionOptions(causal=0))
+    assert api.device_status() == 0
+    for b, h in ((0, 0), (7, 31)):
+        ref = orc.attention(q[b, h].float().cpu().numpy(), k[b, h].float().cpu().numpy(),
+                            v[b, h].float().cpu().numpy(), None, None, 0, nthreads=orc.threads())
+        got = out[b, h].cpu().numpy()
+        err = float(np.abs(got - ref).max()) / float(np.abs(ref).max())
+        assert err <= 5e-3, (b, h, err)
