@@ -541,6 +541,53 @@ def run_reference(args) -> int:
     return 0
 
 
+def run_profile(args) -> int:
+    """Runs one workload a few times (for ncu captures of a single kernel)."""
+    import torch
+
+    from forma_b200 import api
+    from forma_b200.api import AttentionOptions, ConvOptions, ReduceOp
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    name = args.profile
+    if name in ("conv_c3a", "conv_c3b"):
+        cin, k, pad = (256, 3, 1) if name == "conv_c3a" else (1024, 1, 0)
+        x = torch.randn(256, 14, 14, cin, device=dev, generator=g).bfloat16().permute(0, 3, 1, 2)
+        w = (torch.randn(256, k, k, cin, device=dev, generator=g) * 0.02).bfloat16().permute(0, 3, 1, 2)
+        o = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
+        fn = lambda: api.conv_low_f32(x, w, o)  # noqa: E731
+    elif name in ("attn_c4", "attn_c4_small"):
+        b = 8 if name == "attn_c4" else 2
+        q = torch.randn(b, 32, 4096, 128, device=dev, generator=g).bfloat16()
+        k_ = torch.randn(b, 32, 4096, 128, device=dev, generator=g).bfloat16()
+        v = torch.randn(b, 32, 4096, 128, device=dev, generator=g).bfloat16()
+        fn = lambda: api.attention_low_f32(q, k_, v, None, AttentionOptions(causal=0))  # noqa: E731
+    elif name == "conv_c1":
+        x = torch.rand(8, 64, 56, 56, device=dev, generator=g) * 2 - 1
+        w = torch.randn(64, 64, 3, 3, device=dev, generator=g) * 0.06
+        o = ConvOptions([1, 1], [1, 1], [1, 1], [1, 1])
+        fn = lambda: api.conv(x, w, o)  # noqa: E731
+    elif name == "rows_softmax":
+        x = torch.randn(args.rows, COLS, device=dev, generator=g)
+        fn = lambda: api.softmax(x, [1])  # noqa: E731
+    elif name == "rows_argmax":
+        x = torch.randn(args.rows, COLS, device=dev, generator=g)
+        fn = lambda: api.argmax(x, 1)  # noqa: E731
+    elif name == "rows_moments":
+        x = torch.randn(args.rows, COLS, device=dev, generator=g)
+        fn = lambda: api.moments(x, [1])  # noqa: E731
+    else:
+        raise SystemExit(f"unknown profile workload {name}")
+    for _ in range(max(1, args.steps)):
+        fn()
+    torch.cuda.synchronize()
+    status = api.device_status()
+    print(json.dumps({"profile": name, "launches": api.launch_count(), "device_status": status}))
+    return 0 if status == 0 else 1
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -553,11 +600,16 @@ def main(argv=None) -> int:
     ap.add_argument("--no-clocks", action="store_true", help="skip clock sampling (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end pass (profiling runs)")
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
+    ap.add_argument("--profile", default=None,
+                    help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, "
+                         "conv_c1, rows_softmax, rows_argmax, rows_moments)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "forma":
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return run_profile(args)
     return run_forma(args)
 
 
