@@ -102,6 +102,8 @@ SIGNATURES = {
     "fb_argmax": (C.c_int, [T, C.c_uint32, C.c_int32, T, VP]),
     "fb_sum_partial_f64": (C.c_int, [T, VP, VP]),
     "fb_finish_sum_f64": (C.c_int, [VP, T, VP]),
+    "fb_sum_partial_f64_static": (C.c_int, [T, VP, VP]),
+    "fb_sum_static_max_elements": (C.c_uint64, []),
     "fb_softmax": (C.c_int, [T, U32P, C.c_uint32, T, VP]),
     "fb_log_softmax": (C.c_int, [T, U32P, C.c_uint32, T, VP]),
     "fb_logsumexp": (C.c_int, [T, U32P, C.c_uint32, C.c_int32, T, VP]),

@@ -617,6 +617,26 @@ int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream) {
     return launched(launch_sum_partial(rows, partial, stream), "sum partial");
 }
 
+int fb_sum_partial_f64_static(const fb_tensor* input, double* partial, void* stream) {
+    View in;
+    FB_TRY(view_of(input, "input", &in));
+    if (in.dtype != FB_F32) return fail(FB_ERR_DTYPE, "global sum input must be f32");
+    if (!partial) return fail(FB_ERR_INVALID_INPUT, "null partial pointer");
+    if (in.count > static_sum_max_elements())
+        return fail(FB_ERR_INVALID_INPUT, "input has " + std::to_string(in.count) +
+                                              " elements; the static-scratch global sum accepts at most " +
+                                              std::to_string(static_sum_max_elements()));
+    Rows rows = make_rows(in, all_axes(in.dims.size()));
+    if (in.count == 0) {
+        if (cudaMemsetAsync(partial, 0, sizeof(double), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+            return fail(FB_ERR_DRIVER, "memset failed");
+        return FB_OK;
+    }
+    return launched(launch_sum_partial_static(rows, partial, stream), "static-scratch sum partial");
+}
+
+uint64_t fb_sum_static_max_elements(void) { return static_sum_max_elements(); }
+
 int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream) {
     View out;
     FB_TRY(view_of(output, "output", &out));

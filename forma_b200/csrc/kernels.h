@@ -92,6 +92,9 @@ int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const Row
                       float epsilon, void* stream);
 int launch_sum_partial(const Rows& in, double* partial, void* stream);
 int launch_finish_sum(const double* partial, float* out, void* stream);
+// The no-allocation variant: scratch in a static device array (reduce.cu).
+int launch_sum_partial_static(const Rows& in, double* partial, void* stream);
+uint64_t static_sum_max_elements();
 // Writes `count` elements of `value` (f32 or u32 bits) into a dense-permuted output.
 int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream);
 // Copies a strided view into a (dense-permuted) output of the same logical shape.

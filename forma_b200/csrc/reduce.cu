@@ -14,6 +14,7 @@
 // argmax compare total-order keys so they are exact and order-independent.
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "async.cuh"
@@ -727,6 +728,65 @@ int launch_sum_partial(const Rows& in, double* partial, void* stream) {
         sum_partial_kernel<4><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
     else
         sum_partial_kernel<1><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
+    return check_launch();
+}
+
+// Global-sum partial without allocation.  Some callers cannot call
+// cudaMalloc (engines that reserve the device's memory up front and route
+// every allocation through their own pool, and latency-critical paths on
+// which cudaMalloc's implicit device-wide synchronisation is not acceptable),
+// so this variant keeps its block partials and finishing counter in a
+// file-scope device array instead of library-allocated scratch.  The array is
+// FB_SUM_STATIC_SCRATCH_BYTES per device and lives until the process exits;
+// every call shares it and it keeps the last call's contents, so the counter
+// is cleared at the start of each call and calls that overlap on the GPU
+// race.  In host code the array's name is only a host-side stand-in, so its
+// device address is looked up once per device (with that device current) and
+// cached; the first call on each device performs that lookup and should
+// therefore come before any stream capture.
+namespace {
+constexpr uint64_t kStaticCounterBytes = 256;
+constexpr uint64_t kStaticPartials = (FB_SUM_STATIC_SCRATCH_BYTES - kStaticCounterBytes) / sizeof(double);
+constexpr uint64_t kStaticBlockElems = 1ull << 18;  // elements per block of the static variant
+
+static __device__ __align__(256) unsigned char g_sum_static_scratch[FB_SUM_STATIC_SCRATCH_BYTES];
+
+std::mutex g_static_mutex;
+void* g_static_addr[64] = {};
+
+// Device address of g_sum_static_scratch on the current device.
+int static_sum_scratch(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FB_ERR_DRIVER;
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_addr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_sum_static_scratch) != cudaSuccess || !ptr) return FB_ERR_DRIVER;
+        g_static_addr[dev] = ptr;
+    }
+    *out = g_static_addr[dev];
+    return FB_OK;
+}
+}  // namespace
+
+uint64_t static_sum_max_elements() { return kStaticPartials * kStaticBlockElems; }
+
+int launch_sum_partial_static(const Rows& in, double* partial, void* stream) {
+    const uint64_t count = in.cols;
+    const uint64_t blocks = count == 0 ? 1 : (count + kStaticBlockElems - 1) / kStaticBlockElems;
+    if (blocks > kStaticPartials) return FB_ERR_INVALID_INPUT;
+    void* base = nullptr;
+    const int rc = static_sum_scratch(&base);
+    if (rc != FB_OK) return rc;
+    double* partials = static_cast<double*>(base);
+    unsigned* counter =
+        reinterpret_cast<unsigned*>(static_cast<char*>(base) + FB_SUM_STATIC_SCRATCH_BYTES - kStaticCounterBytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess) return FB_ERR_DRIVER;
+    if (vec_ok(in))
+        sum_partial_kernel<4><<<(unsigned)blocks, BLOCK, 0, s>>>(in, partials, counter, partial);
+    else
+        sum_partial_kernel<1><<<(unsigned)blocks, BLOCK, 0, s>>>(in, partials, counter, partial);
     return check_launch();
 }
 

@@ -240,6 +240,26 @@ int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream);
  * element, any rank with numel 1). */
 int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream);
 
+/* Size of the per-device static scratch array of fb_sum_partial_f64_static. */
+#define FB_SUM_STATIC_SCRATCH_BYTES 65536
+
+/* fb_sum_partial_f64 for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Engines that reserve the device's memory up
+ * front and route every allocation through their own pool, and latency-
+ * critical paths on which cudaMalloc's implicit device-wide synchronisation
+ * is not acceptable, cannot let a library call cudaMalloc; this entry point
+ * calls no allocating routine.  Its block partials and finishing counter live
+ * in a file-scope device array of FB_SUM_STATIC_SCRATCH_BYTES that every GPU
+ * loading the library keeps until the process exits.  Limits: one partial
+ * per 2^18 input elements, so inputs above fb_sum_static_max_elements()
+ * elements (about 2.1e9) are rejected with FB_ERR_INVALID_INPUT.  Every call
+ * shares the array (the counter is cleared at the start of each call): calls
+ * that overlap on the GPU, on any stream, race.  The first call on each
+ * device looks up the array's device address (cached afterwards); make that
+ * first call before any stream capture.  Output as fb_sum_partial_f64. */
+int fb_sum_partial_f64_static(const fb_tensor* input, double* partial, void* stream);
+/* Largest input element count fb_sum_partial_f64_static accepts. */
+uint64_t fb_sum_static_max_elements(void);
 
 /* ------------------------------------------------------------- statistics */
 
