@@ -179,7 +179,7 @@ class Dist:
             from datetime import timedelta
 
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=180),
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=60),
                                                  device_id=torch.device("cuda", self.local))
             self.pg = torch.distributed.group.WORLD
 
@@ -363,8 +363,11 @@ def run_forma(args) -> int:
               for k in bytes_per}
     per_kernel_ms = {k: 0.0 for k in bytes_per}
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    class _Local:
+        pg = None  # no collective: ranks may run different numbers of busy steps
+
     def busy():
-        row_ops(api, x, dist)
+        row_ops(api, x, _Local)
         torch.cuda.synchronize(dev)
 
     with ClockSampler(None if args.no_clocks else pci_bus_id(torch, dev), enabled=not args.no_clocks) as clocks:

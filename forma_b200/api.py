@@ -328,9 +328,10 @@ def finish_sum(partial: torch.Tensor, out: Optional[torch.Tensor] = None) -> tor
 
 def global_sum(shard: torch.Tensor, group=None) -> torch.Tensor:
     """Sum over all elements of all ranks' shards: local f64 partial, one
-    all-reduce of 8 bytes when a process group is given, then f32 rounding."""
+    8-byte all-reduce over `group` (only when a group is given: every rank of
+    the group must make the same call), then f32 rounding."""
     partial = sum_partial_f64(shard)
-    if group is not None or (torch.distributed.is_available() and torch.distributed.is_initialized()):
+    if group is not None:
         torch.distributed.all_reduce(partial, group=group)
     return finish_sum(partial)
 

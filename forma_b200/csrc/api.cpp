@@ -25,6 +25,7 @@ const char* last_error_cstr();
 namespace {
 
 std::atomic<uint64_t> g_launches{0};
+thread_local std::string g_driver_error;
 
 struct ScratchBlock {
     void* ptr = nullptr;
@@ -43,7 +44,9 @@ int launched(int status, const char* what) {
     if (status == FB_OK) return FB_OK;
     if (status == FB_ERR_DRIVER) {
         cudaError_t e = cudaGetLastError();
-        return fail(status, std::string(what) + ": " + cudaGetErrorString(e));
+        std::string detail = g_driver_error.empty() ? std::string(cudaGetErrorString(e)) : g_driver_error;
+        g_driver_error.clear();
+        return fail(status, std::string(what) + ": " + detail);
     }
     return fail(status, what);
 }
@@ -450,6 +453,13 @@ int sm_count() {
 }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int launch_status(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return FB_OK;
+    g_driver_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+    return FB_ERR_DRIVER;
+}
 
 void* scratch(void* stream, uint64_t bytes, int slot) {
     int dev = 0;

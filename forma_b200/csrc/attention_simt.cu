@@ -142,7 +142,7 @@ int launch_attention_simt(const AttnArgs& a, void* stream) {
     }
     count_launch();
     if (e != cudaSuccess) return FB_ERR_DRIVER;
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 }  // namespace fb

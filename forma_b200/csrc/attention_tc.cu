@@ -1,21 +1,28 @@
 // Fused flash attention on the 5th-generation tensor cores (tcgen05).
 //
 // attention_low_f32 for 16-bit Q/K/V, depth D in {64, 128}, no mask tensor,
-// optional causal offset.  One CTA owns 128 query rows of one (batch, head):
-//   warp 0      TMA producer: the Q tile once, then K/V tiles of 128 keys
-//               into a 2-stage shared-memory ring (128B-swizzled boxes of 64
-//               depth columns).
-//   warp 1      TMEM allocator and MMA issuer:
-//                 S_j = Q K_j^T  -> TMEM S buffer j%2 (128 x 128 f32)
-//                 O  += P_j V_j  -> TMEM O (128 x D f32), P from shared memory
-//               S_{j+1} is issued before PV_j so the tensor core computes the
-//               next scores while the softmax warps work on the current ones.
-//   warps 2-5   softmax, one query row per thread: tcgen05.ld of the S row,
-//               scale, causal/length mask, row max, exp2, row sum, P packed
-//               to 16-bit into the swizzled K-major tile; the running max is
+// optional causal offset.  One CTA owns 256 query rows (two 128-row Q tiles)
+// of one (batch, head) and streams that head's K/V once for both tiles.
+//   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys
+//               into a 2-stage ring (128B-swizzled boxes of 64 depth columns).
+//   warp 1      TMEM allocator and MMA issuer.  Per key tile j, per Q tile t:
+//                 S_t = Q_t K_j^T  -> TMEM S_t (128 x 128 f32)
+//                 O_t += P_t V_j   -> TMEM O_t (128 x D f32), P_t read from
+//                                     TMEM where it overwrote S_t (tcgen05.mma
+//                                     with the A operand in TMEM)
+//               in the order S_0, S_1, then PV_0, S_0', PV_1, S_1', ... so the
+//               tensor core computes one tile's products while the other
+//               tile's softmax runs (ping-pong).
+//   warps 2-5   softmax of Q tile 0, warps 6-9 of Q tile 1, one query row per
+//               thread: tcgen05.ld of the S row, row max on raw scores, one
+//               FFMA + ex2 per score, running sum, P packed to 16-bit pairs
+//               and written back over S with tcgen05.st.  The running max is
 //               only raised (and O rescaled in TMEM) when a row max exceeds it
 //               by more than 2^8, so P <= 2^8 and rescales are rare.
 //               Finally O / l is written as f32.
+// Ordering: a tcgen05.commit completes only after every earlier MMA of the
+// issuing thread, so "S_t of tile j+1 ready" also certifies that PV_t of tile
+// j has consumed P_t and updated O_t: the softmax needs no other wait.
 // Overflow: BF16 P is stored pre-multiplied by 2^-shift (shift = 9 + log2 of
 // the key count, an exact power of two), so the unnormalised numerator sum P V
 // stays below max|V| and cannot overflow f32 even for V near the format's
@@ -38,13 +45,13 @@ namespace {
 
 __device__ uint32_t g_attn_status;
 
-constexpr int TQ = 128, TK = 128, THREADS = 192;
+constexpr int TQ = 128, TK = 128, QT = 2, THREADS = 64 + QT * 128;
 
 struct AttnParams {
     uint32_t fmt;           // 0 f16, 1 bf16
     uint32_t L, Lk;         // queries, keys per head
     uint32_t H, Hkv;        // query heads, key/value heads
-    uint32_t q_tiles, bh;   // query tiles per head, batch x heads
+    uint32_t q_blocks, bh;  // 256-row query blocks per head, batch x heads
     uint32_t kv_tiles;
     float scale_log2;       // scale * log2(e)
     float shift;            // log2 of the numerator pre-scale
@@ -55,14 +62,16 @@ struct AttnParams {
 template <int D>
 struct ACfg {
     static constexpr int BOXES = D / 64;               // 64-column swizzle boxes per row
-    static constexpr int Q_BYTES = TQ * D * 2;
+    static constexpr int Q_BYTES = TQ * D * 2;         // one Q tile
     static constexpr int K_BYTES = TK * D * 2;
     static constexpr int V_BYTES = TK * D * 2;
     static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-    static constexpr int STAGES = 2;
-    static constexpr int P_BYTES = TQ * TK * 2;
-    static constexpr int SMEM = 1024 + Q_BYTES + STAGES * STAGE_BYTES + P_BYTES + 256;
-    static constexpr uint32_t S_COL = 0, O_COL = 256, TMEM_COLS = 512;
+    static constexpr int STAGES = D == 64 ? 4 : 2;
+    static constexpr int SMEM = 1024 + QT * Q_BYTES + STAGES * STAGE_BYTES + 256;
+    static constexpr uint32_t TMEM_COLS = 512;
+    // TMEM columns: S_t at t*128 (P_t aliases its first 64), O_t at 256 + t*128.
+    static __device__ __forceinline__ uint32_t s_col(int t) { return (uint32_t)(t * TK); }
+    static __device__ __forceinline__ uint32_t o_col(int t) { return (uint32_t)(2 * TK + t * 128); }
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -104,6 +113,16 @@ __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t smem_addr, uint32_t l
     return d;
 }
 
+// Key tiles visible to the 128 query rows starting at q0 (0 if none exist).
+__device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t q0) {
+    if (q0 >= p.L) return 0;
+    if (!p.causal) return p.kv_tiles;
+    const int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
+    const int64_t last_key = last_q + (int64_t)p.causal_offset;
+    const int64_t need = last_key < 0 ? 0 : last_key / TK + 1;
+    return (uint32_t)(need < (int64_t)p.kv_tiles ? need : p.kv_tiles);
+}
+
 template <int D>
 __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
@@ -111,33 +130,31 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
     using C = ACfg<D>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* sQ = smem;
-    unsigned char* sKV = sQ + C::Q_BYTES;
-    unsigned char* sP = sKV + C::STAGES * C::STAGE_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
-    uint64_t* q_full = bars;           // 1
-    uint64_t* kv_full = bars + 1;      // STAGES
-    uint64_t* kv_empty = bars + 3;     // STAGES
-    uint64_t* s_full = bars + 5;       // 2
-    uint64_t* s_free = bars + 7;       // 2
-    uint64_t* p_full = bars + 9;       // 1
-    uint64_t* pv_done = bars + 10;     // 1
-    uint64_t* drain = bars + 11;       // 1
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    unsigned char* sQ = smem;                          // QT tiles
+    unsigned char* sKV = sQ + QT * C::Q_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::STAGES * C::STAGE_BYTES);
+    uint64_t* q_full = bars;                           // 1
+    uint64_t* kv_full = bars + 1;                      // STAGES
+    uint64_t* kv_empty = kv_full + C::STAGES;          // STAGES
+    uint64_t* s_full = kv_empty + C::STAGES;           // QT
+    uint64_t* p_full = s_full + QT;                    // QT
+    uint64_t* o_done = p_full + QT;                    // QT
+    uint64_t* drain = o_done + QT;                     // 1
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // Heaviest (last, for causal) query tiles first.
-    const uint32_t bh = blockIdx.x % p.bh;
-    const uint32_t qt = p.q_tiles - 1 - blockIdx.x / p.bh;
-    const uint32_t q0 = qt * TQ;
-    // Key tiles this query tile can see.
-    uint32_t n_kv = p.kv_tiles;
-    if (p.causal) {
-        const int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
-        const int64_t last_key = last_q + (int64_t)p.causal_offset;
-        const int64_t need = last_key < 0 ? 0 : last_key / TK + 1;
-        n_kv = (uint32_t)(need < (int64_t)p.kv_tiles ? need : p.kv_tiles);
-    }
+    // Consecutive CTAs take the query blocks of one (batch, head), heaviest
+    // (last, for causal) first, so the CTAs in flight share a few heads' K/V
+    // in L2.
+    const uint32_t bh = blockIdx.x / p.q_blocks;
+    const uint32_t qb = p.q_blocks - 1 - blockIdx.x % p.q_blocks;
+    const uint32_t q0 = qb * (QT * TQ);
+    uint32_t n_t[QT];
+#pragma unroll
+    for (int t = 0; t < QT; ++t) n_t[t] = visible_tiles(p, q0 + t * TQ);
+    uint32_t n_kv = 0;
+#pragma unroll
+    for (int t = 0; t < QT; ++t) n_kv = max(n_kv, n_t[t]);
     const uint32_t batch = bh / p.H, head = bh % p.H;
     const uint32_t kv_bh = batch * p.Hkv + head / (p.H / p.Hkv);
     const int32_t q_row0 = (int32_t)(bh * p.L + q0);
@@ -149,12 +166,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&s_full[b], 1);
-            mbar_init(&s_free[b], 128);
+        for (int t = 0; t < QT; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], 128);
+            mbar_init(&o_done[t], 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(pv_done, 1);
         mbar_init(drain, 1);
         fence_barrier_init();
     }
@@ -170,8 +186,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ TMA producer
         if (n_kv > 0) {
-            mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-            for (int b = 0; b < C::BOXES; ++b) tma_load_2d(sQ + b * (TQ * 128), &tmQ, b * 64, q_row0, q_full);
+            mbar_arrive_expect_tx(q_full, QT * C::Q_BYTES);
+            for (int t = 0; t < QT; ++t)
+                for (int b = 0; b < C::BOXES; ++b)
+                    tma_load_2d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, q_row0 + t * TQ, q_full);
         }
         uint32_t issued = 0;
         bool failed = false;
@@ -201,150 +219,164 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         const uint32_t idesc_s = f16_idesc(p.fmt, TQ, TK);
         const uint32_t idesc_o = f16_idesc(p.fmt, TQ, D) | (1u << 16);  // B (V) is MN-major
         bool ok = n_kv == 0 || mbar_wait(q_full, 0);
-        const uint32_t q_addr = smem_u32(sQ);
-        const uint32_t p_addr = smem_u32(sP);
-        auto issue_s = [&](uint32_t j) -> bool {
-            const uint32_t s = j % C::STAGES, b = j & 1;
+        auto issue_s = [&](int t, uint32_t j) -> bool {
+            const uint32_t s = j % C::STAGES;
             if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1)) return false;
-            if (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) / 2) & 1)) return false;
             tc_fence_after();
+            const uint32_t q_addr = smem_u32(sQ + t * C::Q_BYTES);
             const uint32_t k_addr = smem_u32(sKV + s * C::STAGE_BYTES);
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
                 const uint32_t off = (uint32_t)((k / 4) * (TQ * 128) + (k % 4) * 32);
-                umma_f16_ss(tmem + C::S_COL + b * TK, sw128_desc(q_addr + off), sw128_desc(k_addr + off), idesc_s, k != 0);
+                umma_f16_ss(tmem + C::s_col(t), sw128_desc(q_addr + off), sw128_desc(k_addr + off), idesc_s, k != 0);
             }
-            umma_commit(&s_full[b]);
+            umma_commit(&s_full[t]);
             return true;
         };
-        auto issue_pv = [&](uint32_t j) -> bool {
+        auto issue_pv = [&](int t, uint32_t j) -> bool {
             const uint32_t s = j % C::STAGES;
-            if (!mbar_wait(p_full, j & 1)) return false;
+            if (!mbar_wait(&p_full[t], j & 1)) return false;
             tc_fence_after();
             const uint32_t v_addr = smem_u32(sKV + s * C::STAGE_BYTES + C::K_BYTES);
 #pragma unroll
-            for (int k = 0; k < TK / 16; ++k) {
-                const uint32_t poff = (uint32_t)((k / 4) * (TQ * 128) + (k % 4) * 32);
-                umma_f16_ss(tmem + C::O_COL, sw128_desc(p_addr + poff), sw128_mn_desc(v_addr + k * 16 * 128, TK * 128),
+            for (int k = 0; k < TK / 16; ++k)
+                umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + k * 8, sw128_mn_desc(v_addr + k * 16 * 128, TK * 128),
                             idesc_o, (j | k) != 0);
-            }
-            umma_commit(pv_done);
-            umma_commit(&kv_empty[s]);
+            if (j + 1 == n_t[t]) umma_commit(&o_done[t]);
             return true;
         };
-        if (ok && n_kv > 0) ok = issue_s(0);
+        for (int t = 0; t < QT && ok; ++t)
+            if (n_t[t] > 0) ok = issue_s(t, 0);
         for (uint32_t j = 0; ok && j < n_kv; ++j) {
-            if (j + 1 < n_kv) ok = issue_s(j + 1);
-            if (ok) ok = issue_pv(j);
+            for (int t = 0; t < QT && ok; ++t) {
+                if (j >= n_t[t]) continue;
+                ok = issue_pv(t, j);
+                if (ok && j + 1 < n_t[t]) ok = issue_s(t, j + 1);
+            }
+            // stage j is free once every PV reading it has completed
+            if (ok) umma_commit(&kv_empty[j % C::STAGES]);
         }
         if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
         umma_commit(drain);
         (void)mbar_wait(drain, 0);
     } else if (warp >= 2) {
         // ------------------------------------------------ softmax / epilogue
+        const int t = (warp - 2) / 4;                  // Q tile of this warpgroup
         const int quarter = warp & 3;
         const uint32_t row = (uint32_t)(quarter * 32 + lane);
-        const uint32_t q = q0 + row;
+        const uint32_t q = q0 + t * TQ + row;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        const uint32_t n = n_t[t];
         const int64_t vis = p.causal ? (int64_t)q + (int64_t)p.causal_offset : (int64_t)1 << 40;
-        float m_used = -__int_as_float(0x7f800000);  // running max (log2 units)
+        const float NEG = -__int_as_float(0x7f800000);
+        const float sl = p.scale_log2;
+        float m_used = NEG;  // running max (log2 units)
         float l = 0.0f;
         bool ok = true;
-        unsigned char* prow = sP + row * 128;
-        const uint32_t sw = row & 7;
-        for (uint32_t j = 0; j < n_kv && ok; ++j) {
-            const uint32_t b = j & 1;
+        for (uint32_t j = 0; j < n && ok; ++j) {
             // Wait outcomes are made warp-uniform: tcgen05.ld/st are .sync.aligned.
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j / 2) & 1))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             float x[TK];
             {
-                uint32_t r[32];
+                uint32_t r[TK];
 #pragma unroll
-                for (int c = 0; c < TK / 32; ++c) {
-                    tmem_ld32(tmem + lane_base + C::S_COL + b * TK + c * 32, r);
-                    tmem_wait_ld();
+                for (int c = 0; c < TK / 32; ++c)
+                    tmem_ld32(tmem + lane_base + C::s_col(t) + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+                tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
-                }
+                for (int i = 0; i < TK; ++i) x[i] = __uint_as_float(r[i]);
             }
-            tc_fence_before();
-            mbar_arrive(&s_free[b]);
-            // scale into log2 units and mask keys beyond the length / causal edge
+            // Keys past the length or the causal edge are masked only in the
+            // tiles that reach them; logits are x * sl, so the row maximum of
+            // the logits is the maximum of x (sl > 0) or its minimum (sl < 0).
             const int64_t key0 = (int64_t)j * TK;
-            float mt = -__int_as_float(0x7f800000);
+            const bool edge = key0 + TK > (int64_t)p.Lk || key0 + TK - 1 > vis;
+            if (edge || sl == 0.0f) {
+                const int64_t lim64 = min((int64_t)p.Lk - key0, vis - key0 + 1);
+                const int32_t lim = (int32_t)(lim64 < 0 ? 0 : (lim64 > TK ? TK : lim64));
 #pragma unroll
-            for (int i = 0; i < TK; ++i) {
-                const int64_t key = key0 + i;
-                const bool visible = key < (int64_t)p.Lk && key <= vis;
-                x[i] = visible ? x[i] * p.scale_log2 : -__int_as_float(0x7f800000);
-                mt = fmaxf(mt, x[i]);
+                for (int i = 0; i < TK; ++i) x[i] = i < lim ? x[i] * sl : NEG;  // logits, masked
             }
+            const bool raw = !(edge || sl == 0.0f);
+            const bool use_min = raw && sl < 0.0f;
+            float mx[8];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) mx[a] = x[a];
+            if (use_min) {
+#pragma unroll
+                for (int i = 8; i < TK; ++i) mx[i & 7] = fminf(mx[i & 7], x[i]);
+            } else {
+#pragma unroll
+                for (int i = 8; i < TK; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+            }
+            float mt = use_min ? fminf(fminf(fminf(mx[0], mx[1]), fminf(mx[2], mx[3])), fminf(fminf(mx[4], mx[5]), fminf(mx[6], mx[7])))
+                               : fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            if (raw) mt *= sl;  // raw extreme -> logit maximum
             float alpha = 1.0f;
             bool rescale = false;
             if (mt > m_used + 8.0f) {
-                alpha = m_used == -__int_as_float(0x7f800000) ? 0.0f : ex2(m_used - mt);
+                alpha = m_used == NEG ? 0.0f : ex2(m_used - mt);
                 rescale = j > 0 && l > 0.0f;
                 m_used = mt;
             }
-            // PV_{j-1} must be done before P is overwritten or O rescaled.
-            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1))) {
-                ok = false;
-                break;
+            const float base = m_used == NEG ? 0.0f : m_used + p.shift;
+            // P = exp2(logit - base): one FFMA + ex2 per score on the raw path.
+            float lsa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            // Packed pairs overwrite the scores they came from (element i of
+            // a chunk is written after elements 2i and 2i+1 were read), so P
+            // needs no registers of its own.
+            uint32_t* xb = reinterpret_cast<uint32_t*>(x);
+#pragma unroll
+            for (int c = 0; c < TK / 32; ++c) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float a0 = x[c * 32 + 2 * i], a1 = x[c * 32 + 2 * i + 1];
+                    const float e0 = raw ? ex2(fmaf(a0, sl, -base)) : ex2(a0 - base);
+                    const float e1 = raw ? ex2(fmaf(a1, sl, -base)) : ex2(a1 - base);
+                    lsa[(2 * i) & 7] += e0;
+                    lsa[(2 * i + 1) & 7] += e1;
+                    xb[c * 32 + i] = pack2(e0, e1, p.fmt);
+                }
+                tmem_st16(tmem + lane_base + C::s_col(t) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&xb[c * 32]));
             }
-            tc_fence_after();
             if (rescale) {
+                // After P is out of the score registers: O_t is quiescent (S_t
+                // of this tile completed after PV_t of the previous one, and
+                // PV_t of this tile waits for the arrival below).
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t r[32];
-                    tmem_ld32(tmem + lane_base + C::O_COL + c * 32, r);
+                    tmem_ld32(tmem + lane_base + C::o_col(t) + c * 32, r);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st32(tmem + lane_base + C::O_COL + c * 32, r);
+                    tmem_st32(tmem + lane_base + C::o_col(t) + c * 32, r);
                 }
-                tmem_wait_st();
             }
-            const float base = m_used == -__int_as_float(0x7f800000) ? 0.0f : m_used + p.shift;
-            float ls = 0.0f;
-#pragma unroll
-            for (int c = 0; c < TK / 8; ++c) {
-                float e[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    e[i] = ex2(x[c * 8 + i] - base);
-                    ls += e[i];
-                }
-                uint4 v;
-                v.x = pack2(e[0], e[1], p.fmt);
-                v.y = pack2(e[2], e[3], p.fmt);
-                v.z = pack2(e[4], e[5], p.fmt);
-                v.w = pack2(e[6], e[7], p.fmt);
-                const uint32_t atom = (uint32_t)(c / 8), chunk = (uint32_t)(c % 8);
-                *reinterpret_cast<uint4*>(prow + atom * (TQ * 128) + ((chunk ^ sw) << 4)) = v;
-            }
+            tmem_wait_st();
+            const float ls = ((lsa[0] + lsa[1]) + (lsa[2] + lsa[3])) + ((lsa[4] + lsa[5]) + (lsa[6] + lsa[7]));
             l = l * alpha + ls;
-            fence_proxy_async_smem();  // P written by generic stores, read by the tensor core
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[t]);
         }
         // epilogue: O / l, f32 rows
-        if (ok && n_kv > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (n_kv - 1) & 1))) ok = false;
+        if (ok && n > 0 && !__all_sync(0xffffffffu, mbar_wait(&o_done[t], 0))) ok = false;
         if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
         tc_fence_after();
-        // `ok` and n_kv are warp-uniform here, so the loads below are too; only
-        // the stores depend on whether this row exists (q < L).
-        const bool load = ok && n_kv > 0;
+        // `ok` and n are warp-uniform, so the loads are too; only the stores
+        // depend on whether this row exists (q < L).
+        const bool load = ok && n > 0;
         float* orow = p.out + ((uint64_t)bh * p.L + q) * D;
         const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
             if (load) {
-                tmem_ld32(tmem + lane_base + C::O_COL + c * 32, r);
+                tmem_ld32(tmem + lane_base + C::o_col(t) + c * 32, r);
                 tmem_wait_ld();
             } else {
 #pragma unroll
@@ -432,7 +464,7 @@ int launch_d(const AttnArgs& a, uint32_t fmt, cudaStream_t st) {
     p.Lk = (uint32_t)Lk;
     p.H = (uint32_t)H;
     p.Hkv = (uint32_t)Hkv;
-    p.q_tiles = (uint32_t)((L + TQ - 1) / TQ);
+    p.q_blocks = (uint32_t)((L + QT * TQ - 1) / (QT * TQ));
     p.bh = (uint32_t)BH;
     p.kv_tiles = (uint32_t)((Lk + TK - 1) / TK);
     p.scale_log2 = a.scale * 1.4426950408889634f;
@@ -446,13 +478,13 @@ int launch_d(const AttnArgs& a, uint32_t fmt, cudaStream_t st) {
     p.out = a.out + a.o_offset;
     auto kernel = attn_fwd_kernel<D>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-        return FB_ERR_DRIVER;
-    const uint64_t grid = (uint64_t)p.q_tiles * BH;
+        return launch_status("shared-memory attribute");
+    const uint64_t grid = (uint64_t)p.q_blocks * BH;
     if (grid == 0) return FB_OK;
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
     kernel<<<(unsigned)grid, THREADS, C::SMEM, st>>>(tq, tk, tv, p);
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 }  // namespace

@@ -182,7 +182,7 @@ int launch_conv_direct(const ConvArgs& a, void* stream) {
         default: return FB_ERR_DTYPE;
     }
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 int launch_conv2d_f32_tiled(const ConvArgs& a, void* stream) {
@@ -207,7 +207,7 @@ int launch_conv2d_f32_tiled(const ConvArgs& a, void* stream) {
     else
         conv2d_f32_tiled_kernel<1, 1><<<(unsigned)blocks, T_THREADS, 0, s>>>(a);
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 }  // namespace fb

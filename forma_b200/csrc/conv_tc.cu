@@ -310,12 +310,12 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams
     using C = Cfg<BN>;
     auto kernel = conv_gemm_kernel<BN>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-        return FB_ERR_DRIVER;
+        return launch_status("shared-memory attribute");
     const uint32_t tiles = p.m_tiles * p.n_tiles;
     const uint32_t grid = tiles < (uint32_t)sm_count() ? tiles : (uint32_t)sm_count();
     kernel<<<grid, THREADS, C::SMEM, st>>>(ta, tb, p);
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 }  // namespace

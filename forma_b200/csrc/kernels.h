@@ -80,6 +80,9 @@ enum ScratchSlot : int {
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
 void count_launch();
+// Records the pending CUDA error (if any) with `what` as this thread's driver
+// error detail and returns FB_OK when there was none, FB_ERR_DRIVER otherwise.
+int launch_status(const char* what);
 
 // Per translation unit: reads and clears the device status word.
 uint32_t read_reduce_status();

@@ -582,7 +582,7 @@ unsigned grid_for(uint64_t work, unsigned per_sm = 8) {
 
 int check_launch() {
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? FB_OK : FB_ERR_DRIVER;
+    return launch_status("kernel launch");
 }
 
 bool vec_ok(const Rows& in) {
