@@ -15,8 +15,10 @@
 //               tile's softmax runs (ping-pong).
 //   warps 2-5   softmax of Q tile 0, warps 6-9 of Q tile 1, one query row per
 //               thread: tcgen05.ld of the S row, row max on raw scores, one
-//               FFMA + ex2 per score, running sum, P packed to 16-bit pairs
-//               and written back over S with tcgen05.st.  The running max is
+//               FFMA + exp2 per score (three in four on MUFU ex2, one in four
+//               as a polynomial on the FMA pipe), running sum, P packed to
+//               16-bit pairs with integer ops (BF16) and written back over S
+//               with tcgen05.st.  The running max is
 //               only raised (and O rescaled in TMEM) when a row max exceeds it
 //               by more than 2^8, so P <= 2^8 and rescales are rare.
 //               Finally O / l is written as f32.
@@ -78,6 +80,35 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA/ALU pipes, for a share of the softmax exponentials so that
+// the transcendental unit (MUFU ex2) is not the only engine producing them.
+// Cody-Waite split x = n + f: n is the nearest integer, obtained by adding and
+// subtracting 1.5 * 2^23, and |f| <= 1/2; 2^f comes from a degree-4 polynomial
+// whose coefficients were fitted for minimal relative error on [-1/2, 1/2] by
+// iteratively reweighted least squares (max relative error 2.7e-6, far below
+// the 2^-9 rounding of a 16-bit P); n is added to the exponent field.  Inputs
+// below -126 (including -inf for masked scores) give exactly 0.
+__device__ __forceinline__ float ex2_poly(float x) {
+    const float xc = fmaxf(x, -127.0f);
+    const float t = xc + 12582912.0f;
+    const float n = t - 12582912.0f;
+    const float f = xc - n;
+    float q = fmaf(0.009570101276040077f, f, 0.05591785907745361f);
+    q = fmaf(q, f, 0.240247443318367f);
+    q = fmaf(q, f, 0.6931217908859253f);
+    q = fmaf(q, f, 0.9999992847442627f);
+    const int ni = __float_as_int(t) - __float_as_int(12582912.0f);
+    const float r = __int_as_float(__float_as_int(q) + (ni << 23));
+    return x < -126.0f ? 0.0f : r;
+}
+
+// Two non-negative f32 values to a BF16 pair (lo in the low half) with integer
+// operations: round half up (+0x8000, then the high halves by byte permute).
+// Keeps the conversion off the transcendental pipe that ex2 uses.
+__device__ __forceinline__ uint32_t pack_bf16_pos(float lo, float hi) {
+    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, uint32_t fmt) {
@@ -335,11 +366,14 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float a0 = x[c * 32 + 2 * i], a1 = x[c * 32 + 2 * i + 1];
-                    const float e0 = raw ? ex2(fmaf(a0, sl, -base)) : ex2(a0 - base);
-                    const float e1 = raw ? ex2(fmaf(a1, sl, -base)) : ex2(a1 - base);
+                    const float z0 = raw ? fmaf(a0, sl, -base) : a0 - base;
+                    const float z1 = raw ? fmaf(a1, sl, -base) : a1 - base;
+                    // one pair in four on the FMA pipe, the rest on MUFU
+                    const float e0 = (i & 3) == 3 ? ex2_poly(z0) : ex2(z0);
+                    const float e1 = (i & 3) == 3 ? ex2_poly(z1) : ex2(z1);
                     lsa[(2 * i) & 7] += e0;
                     lsa[(2 * i + 1) & 7] += e1;
-                    xb[c * 32 + i] = pack2(e0, e1, p.fmt);
+                    xb[c * 32 + i] = p.fmt ? pack_bf16_pos(e0, e1) : pack2(e0, e1, 0);
                 }
                 tmem_st16(tmem + lane_base + C::s_col(t) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&xb[c * 32]));
             }
