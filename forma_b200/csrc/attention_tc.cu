@@ -14,12 +14,12 @@
 //               tensor core computes one tile's products while the other
 //               tile's softmax runs (ping-pong).
 //   warps 2-5   softmax of Q tile 0, warps 6-9 of Q tile 1, one query row per
-//               thread: tcgen05.ld of the S row, row max on raw scores, one
-//               FFMA + exp2 per score (three in four on MUFU ex2, one in four
-//               as a polynomial on the FMA pipe), running sum, P packed to
-//               16-bit pairs with integer ops (BF16) and written back over S
-//               with tcgen05.st.  The running max is
-//               only raised (and O rescaled in TMEM) when a row max exceeds it
+//               thread: tcgen05.ld of the S row, row max on raw scores (three-
+//               input extremes), one FFMA per score, exp2 (seven pairs in
+//               eight on MUFU ex2, one as a paired polynomial on the FMA pipe),
+//               paired running sums, P packed to 16-bit pairs with integer ops
+//               (BF16) and written back over S with tcgen05.st.  The running max is only
+//               raised (and O rescaled in TMEM) when a row max exceeds it
 //               by more than 2^8, so P <= 2^8 and rescales are rare.
 //               Finally O / l is written as f32.
 // Ordering: a tcgen05.commit completes only after every earlier MMA of the
@@ -82,26 +82,44 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 2^x on the FMA/ALU pipes, for a share of the softmax exponentials so that
-// the transcendental unit (MUFU ex2) is not the only engine producing them.
-// Cody-Waite split x = n + f: n is the nearest integer, obtained by adding and
-// subtracting 1.5 * 2^23, and |f| <= 1/2; 2^f comes from a degree-4 polynomial
-// whose coefficients were fitted for minimal relative error on [-1/2, 1/2] by
-// iteratively reweighted least squares (max relative error 2.7e-6, far below
-// the 2^-9 rounding of a 16-bit P); n is added to the exponent field.  Inputs
-// below -126 (including -inf for masked scores) give exactly 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-    const float xc = fmaxf(x, -127.0f);
-    const float t = xc + 12582912.0f;
-    const float n = t - 12582912.0f;
-    const float f = xc - n;
-    float q = fmaf(0.009570101276040077f, f, 0.05591785907745361f);
-    q = fmaf(q, f, 0.240247443318367f);
-    q = fmaf(q, f, 0.6931217908859253f);
-    q = fmaf(q, f, 0.9999992847442627f);
-    const int ni = __float_as_int(t) - __float_as_int(12582912.0f);
-    const float r = __int_as_float(__float_as_int(q) + (ni << 23));
-    return x < -126.0f ? 0.0f : r;
+// 2^x for a pair of values on the FMA/ALU pipes, for a share of the softmax
+// exponentials so that the transcendental unit (MUFU ex2) is not the only
+// engine producing them.  Cody-Waite split x = n + f: n is the nearest
+// integer, obtained by adding and subtracting 1.5 * 2^23, and |f| <= 1/2; 2^f
+// comes from a degree-3 polynomial whose coefficients minimise the maximum
+// relative error on [-1/2, 1/2] (a linear program over a dense grid; 7.5e-5,
+// below the 2^-11 rounding of an F16 P and the 2^-9 of a BF16 one); n is
+// added to the exponent field (the low 9 bits of t's pattern hold n mod 512).
+// Inputs are clamped to -127 first; at n = -127 a polynomial value below 1
+// carries its exponent field below zero, which the final max with 0 turns
+// into exactly 0, so -inf (a masked score) gives 0 and a fully masked row
+// keeps a zero sum.  The f32x2 forms process both values in one instruction.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    const float2 M = make_float2(12582912.0f, 12582912.0f);
+    const float2 xc = make_float2(fmaxf(x.x, -127.0f), fmaxf(x.y, -127.0f));
+    const float2 t = __fadd2_rn(xc, M);
+    const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), xc);  // exact: xc - n
+    float2 q = __ffma2_rn(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                          make_float2(0.2426111251115799f, 0.2426111251115799f));
+    q = __ffma2_rn(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    q = __ffma2_rn(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+    const int bx = (int)(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23));
+    const int by = (int)(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
+    return make_float2(__int_as_float(max(bx, 0)), __int_as_float(max(by, 0)));
+}
+
+// Three-input extremes that propagate NaN, so a NaN score makes the whole
+// row's base NaN, as an elementwise max/exp/sum over the row would.
+__device__ __forceinline__ float max3n(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float min3n(float a, float b, float c) {
+    float d;
+    asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // Two non-negative f32 values to a BF16 pair (lo in the low half) with integer
@@ -334,18 +352,25 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             }
             const bool raw = !(edge || sl == 0.0f);
             const bool use_min = raw && sl < 0.0f;
-            float mx[8];
-#pragma unroll
-            for (int a = 0; a < 8; ++a) mx[a] = x[a];
+            // Four chains of three-input extremes: 64 instructions per row.
+            float mx[4] = {x[0], x[1], x[2], x[3]};
             if (use_min) {
 #pragma unroll
-                for (int i = 8; i < TK; ++i) mx[i & 7] = fminf(mx[i & 7], x[i]);
+                for (int i = 4; i < TK - 4; i += 8)
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) mx[a] = min3n(mx[a], x[i + 2 * a], x[i + 2 * a + 1]);
+                mx[0] = min3n(mx[0], x[TK - 4], x[TK - 3]);
+                mx[1] = min3n(mx[1], x[TK - 2], x[TK - 1]);
             } else {
 #pragma unroll
-                for (int i = 8; i < TK; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+                for (int i = 4; i < TK - 4; i += 8)
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) mx[a] = max3n(mx[a], x[i + 2 * a], x[i + 2 * a + 1]);
+                mx[0] = max3n(mx[0], x[TK - 4], x[TK - 3]);
+                mx[1] = max3n(mx[1], x[TK - 2], x[TK - 1]);
             }
-            float mt = use_min ? fminf(fminf(fminf(mx[0], mx[1]), fminf(mx[2], mx[3])), fminf(fminf(mx[4], mx[5]), fminf(mx[6], mx[7])))
-                               : fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            float mt = use_min ? min3n(min3n(mx[0], mx[1], mx[2]), mx[3], mx[3])
+                               : max3n(max3n(mx[0], mx[1], mx[2]), mx[3], mx[3]);
             if (raw) mt *= sl;  // raw extreme -> logit maximum
             float alpha = 1.0f;
             bool rescale = false;
@@ -355,8 +380,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
                 m_used = mt;
             }
             const float base = m_used == NEG ? 0.0f : m_used + p.shift;
-            // P = exp2(logit - base): one FFMA + ex2 per score on the raw path.
-            float lsa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            // P = exp2(logit - base): one FFMA per score on the raw path, then
+            // ex2 on MUFU for seven pairs in eight and the paired polynomial
+            // for the eighth.
+            float2 lsa[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             // Packed pairs overwrite the scores they came from (element i of
             // a chunk is written after elements 2i and 2i+1 were read), so P
             // needs no registers of its own.
@@ -365,34 +392,34 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             for (int c = 0; c < TK / 32; ++c) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float a0 = x[c * 32 + 2 * i], a1 = x[c * 32 + 2 * i + 1];
-                    const float z0 = raw ? fmaf(a0, sl, -base) : a0 - base;
-                    const float z1 = raw ? fmaf(a1, sl, -base) : a1 - base;
-                    // one pair in four on the FMA pipe, the rest on MUFU
-                    const float e0 = (i & 3) == 3 ? ex2_poly(z0) : ex2(z0);
-                    const float e1 = (i & 3) == 3 ? ex2_poly(z1) : ex2(z1);
-                    lsa[(2 * i) & 7] += e0;
-                    lsa[(2 * i + 1) & 7] += e1;
-                    xb[c * 32 + i] = p.fmt ? pack_bf16_pos(e0, e1) : pack2(e0, e1, 0);
+                    const float2 a = make_float2(x[c * 32 + 2 * i], x[c * 32 + 2 * i + 1]);
+                    const float2 z = raw ? make_float2(fmaf(a.x, sl, -base), fmaf(a.y, sl, -base)) : make_float2(a.x - base, a.y - base);
+                    const float2 e = (i & 7) == 7 ? ex2_poly2(z) : make_float2(ex2(z.x), ex2(z.y));
+                    lsa[i & 3] = __fadd2_rn(lsa[i & 3], e);
+                    xb[c * 32 + i] = p.fmt ? pack_bf16_pos(e.x, e.y) : pack2(e.x, e.y, 0);
                 }
                 tmem_st16(tmem + lane_base + C::s_col(t) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&xb[c * 32]));
             }
-            if (rescale) {
+            if (__any_sync(0xffffffffu, rescale)) {
                 // After P is out of the score registers: O_t is quiescent (S_t
                 // of this tile completed after PV_t of the previous one, and
-                // PV_t of this tile waits for the arrival below).
+                // PV_t of this tile waits for the arrival below).  The whole
+                // warp takes this branch (tcgen05.ld/st are .sync.aligned);
+                // rows that keep their maximum scale by 1.
+                const float f = rescale ? alpha : 1.0f;
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(tmem + lane_base + C::o_col(t) + c * 32, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
                     tmem_st32(tmem + lane_base + C::o_col(t) + c * 32, r);
                 }
             }
             tmem_wait_st();
-            const float ls = ((lsa[0] + lsa[1]) + (lsa[2] + lsa[3])) + ((lsa[4] + lsa[5]) + (lsa[6] + lsa[7]));
+            const float2 l2 = __fadd2_rn(__fadd2_rn(lsa[0], lsa[1]), __fadd2_rn(lsa[2], lsa[3]));
+            const float ls = l2.x + l2.y;
             l = l * alpha + ls;
             tc_fence_before();
             mbar_arrive(&p_full[t]);
