@@ -333,6 +333,18 @@ def run_ops(api, dev, dist, args, pk) -> dict:
            4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
            "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2")
     del q, k, v
+    # C5: ViT-style encoder forward, [64,3,224,224] bf16, patch 16, 12 layers (E 768, H 12, D 64, L 197, MLP 3072)
+    from forma_b200.vit import ViTConfig, ViTEncoder
+
+    cfg = ViTConfig()
+    enc = ViTEncoder(cfg, dev, seed=dist.rank)
+    img = torch.randn(cfg.batch, cfg.channels, cfg.image, cfg.image, device=dev, generator=g).bfloat16()
+    fl = cfg.flops()
+    record("vit_encoder_c5", lambda: enc.forward(img), fl["total"], pk["bf16_tflops"], "measured bf16 dense (burst)",
+           "random-init pre-norm encoder, LN eps 1e-5, tanh GELU; FLOPs = patch conv + per layer QKV/out/MLP "
+           "projections (1x1 convs) + attention 4*B*H*L^2*D; glue (casts, adds, LN) counted as time only")
+    res["vit_encoder_c5"]["flops_by_stage"] = fl
+    del enc, img
     return res
 
 

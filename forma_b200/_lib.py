@@ -110,6 +110,8 @@ SIGNATURES = {
     "fb_moments": (C.c_int, [T, U32P, C.c_uint32, C.c_int32, T, T, VP]),
     "fb_layer_norm": (C.c_int, [T, U32P, C.c_uint32, C.c_float, T, VP]),
     "fb_cast_to_low": (C.c_int, [T, T, VP]),
+    "fb_add": (C.c_int, [T, T, T, VP]),
+    "fb_gelu_to_low": (C.c_int, [T, T, VP]),
 }
 
 _lib = None

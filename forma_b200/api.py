@@ -398,6 +398,34 @@ def cast_to_low(input: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return out
 
 
+def cast_to_low_into(input: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """cast_to_low into a caller-owned contiguous tensor (chains reuse buffers)."""
+    di, do = describe(input), describe(out)
+    _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(_device(input, out))))
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = a + b (f32), operands of out's shape with any strides (expand() broadcasts).
+
+    Elementwise glue for chained workloads (residual additions); ``out`` may
+    be ``a`` or ``b`` itself when that operand is contiguous."""
+    if out is None:
+        out = torch.empty(list(a.shape), dtype=torch.float32, device=_device(a, b))
+    da, db, do = describe(a), describe(b), describe(out)
+    _check(lib().fb_add(C.byref(da), C.byref(db), C.byref(do), _stream(_device(a, b, out))))
+    return out
+
+
+def gelu_to_low(input: torch.Tensor, dtype: torch.dtype, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """tanh-form GELU of an f32 tensor, rounded once to f16/bf16 (contiguous result)."""
+    if out is None:
+        out = torch.empty(list(input.shape), dtype=dtype, device=_device(input))
+    di, do = describe(input), describe(out)
+    _check(lib().fb_gelu_to_low(C.byref(di), C.byref(do), _stream(_device(input, out))))
+    return out
+
+
 def device_status() -> int:
     """Synchronises and returns (and clears) the mask of timed-out bounded waits."""
     return int(lib().fb_device_status())

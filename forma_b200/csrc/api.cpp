@@ -691,4 +691,68 @@ int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream) {
                     "cast");
 }
 
+int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stream) {
+    View x, y, out;
+    FB_TRY(view_of(a, "a", &x));
+    FB_TRY(view_of(b, "b", &y));
+    FB_TRY(view_of(output, "output", &out));
+    if (x.dtype != FB_F32 || y.dtype != FB_F32 || out.dtype != FB_F32) return fail(FB_ERR_DTYPE, "add needs f32 operands");
+    if (x.dims != out.dims || y.dims != out.dims) return fail(FB_ERR_INVALID_INPUT, "add operand dims differ from output");
+    if (out.count == 0) return FB_OK;
+    // The output may be any layout that gives every element its own address:
+    // non-unit axes sorted by stride, each stride at least the extent of the
+    // axes inside it.
+    {
+        std::vector<std::pair<uint64_t, uint64_t>> ax;
+        for (size_t i = 0; i < out.dims.size(); ++i)
+            if (out.dims[i] > 1) ax.push_back({out.strides[i], out.dims[i]});
+        std::sort(ax.begin(), ax.end());
+        uint64_t extent = 1;
+        for (auto& e : ax) {
+            if (e.first < extent) return fail(FB_ERR_INVALID_INPUT, "add output layout must address each element once");
+            extent = e.first * e.second;
+        }
+    }
+    // An operand may share memory with the output only as the identical view.
+    auto same_view = [&](const View& v) {
+        return v.data == out.data && v.offset == out.offset && v.strides == out.strides;
+    };
+    auto extent_of = [](const View& v) {
+        uint64_t e = 1;
+        for (size_t i = 0; i < v.dims.size(); ++i) e += (v.dims[i] - 1) * v.strides[i];
+        return e;
+    };
+    const uint64_t out_lo = out.offset, out_hi = out.offset + extent_of(out);
+    auto overlaps = [&](const View& v) {
+        if (v.data != out.data || same_view(v)) return false;
+        const uint64_t lo = v.offset, hi = v.offset + extent_of(v);
+        return lo < out_hi && out_lo < hi;
+    };
+    if (overlaps(x) || overlaps(y)) return fail(FB_ERR_INVALID_INPUT, "add operand overlaps the output");
+    const float* xa = static_cast<const float*>(x.data);
+    const float* ya = static_cast<const float*>(y.data);
+    float* o = static_cast<float*>(out.data);
+    const bool dense = is_contiguous(x) && is_contiguous(y) && is_contiguous(out) && out.count % 4 == 0 &&
+                       reinterpret_cast<uintptr_t>(xa + x.offset) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(ya + y.offset) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(o + out.offset) % 16 == 0;
+    Nest xn = make_nest(x.dims, x.strides, all_axes(x.dims.size()));
+    Nest yn = make_nest(y.dims, y.strides, all_axes(y.dims.size()));
+    Nest on = make_nest(out.dims, out.strides, all_axes(out.dims.size()));
+    return launched(launch_add(xa, x.offset, xn, ya, y.offset, yn, o, out.offset, on, out.count, dense, stream), "add");
+}
+
+int fb_gelu_to_low(const fb_tensor* input, fb_tensor* output, void* stream) {
+    View in, out;
+    FB_TRY(view_of(input, "input", &in));
+    FB_TRY(view_of(output, "output", &out));
+    if (in.dtype != FB_F32 || !is_low(out.dtype)) return fail(FB_ERR_DTYPE, "gelu_to_low needs f32 -> f16/bf16");
+    if (out.dims != in.dims) return fail(FB_ERR_INVALID_INPUT, "gelu output dims differ from input");
+    if (!is_contiguous(out)) return fail(FB_ERR_INVALID_INPUT, "gelu output must be contiguous");
+    Nest n = make_nest(in.dims, in.strides, all_axes(in.dims.size()));
+    return launched(launch_gelu_to_low(static_cast<const float*>(in.data), in.offset, n,
+                                       static_cast<uint16_t*>(out.data) + out.offset, out.dtype, in.count, stream),
+                    "gelu");
+}
+
 }  // extern "C"

@@ -42,6 +42,7 @@ struct ConvGemmParams {
     uint32_t k_blocks, c_blocks, S;
     int32_t pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
     uint32_t m_tiles, n_tiles;
+    uint32_t c_rows;  // 1: channels contiguous (s_c == 1) and 16-byte aligned rows
     float* out;
     uint64_t out_offset, s_n, s_c, s_p, s_q;
 };
@@ -53,7 +54,12 @@ struct Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : 8;
     static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;  // align slack + ring + barriers
+    // Epilogue staging for channels-contiguous outputs: per epilogue warp a
+    // 32 x 32 f32 block with rows padded to 36 floats (16-byte aligned rows,
+    // conflict-free float4 writes and reads).
+    static constexpr int EPI_PITCH = 36;
+    static constexpr int EPI_BYTES = 4 * 32 * EPI_PITCH * 4;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;  // align slack + ring + staging + barriers
 };
 
 template <int BN>
@@ -64,7 +70,8 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* ring = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
     uint64_t* full = bars;                     // [STAGES]
     uint64_t* empty = bars + C::STAGES;        // [STAGES]
     uint64_t* tfull = bars + 2 * C::STAGES;    // [2]
@@ -207,14 +214,43 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                        (uint64_t)(nt * BN) * p.s_c;
             }
             const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
+            if (p.c_rows) {
+                // Channels contiguous: each row's 32-column chunk is 128
+                // contiguous bytes.  Stage the warp's 32 x 32 block in shared
+                // memory, then store it as float4 so that one instruction
+                // writes four whole 128-byte rows (8 lanes per row).
+                float* st = epi + quarter * (32 * C::EPI_PITCH);
+                const uint64_t my_base = base ? (uint64_t)(base - p.out) : ~0ull;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + c0, v);
-                tmem_wait_ld();
-                if (base) {
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) base[(uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4*>(st + lane * C::EPI_PITCH + 4 * q) =
+                            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                        __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + (lane >> 3), cc = lane & 7;
+                        const uint64_t rb = __shfl_sync(0xffffffffu, my_base, r);
+                        const float4 val = *reinterpret_cast<const float4*>(st + r * C::EPI_PITCH + 4 * cc);
+                        if (rb != ~0ull) *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
+                    }
+                    __syncwarp();
+                }
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
+                    if (base) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) base[(uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                    }
                 }
             }
             tc_fence_before();
@@ -305,6 +341,44 @@ __global__ void weights_to_ohwi_kernel(const E* w, uint64_t off, uint64_t so, ui
     }
 }
 
+// Weights into dense [O, C, kh, kw] rows (the K order of gathered patches).
+template <typename E>
+__global__ void weights_to_oihw_kernel(const E* w, uint64_t off, uint64_t so, uint64_t sc, uint64_t sr, uint64_t ss,
+                                       uint32_t O, uint32_t Cc, uint32_t R, uint32_t S, E* out) {
+    const uint64_t total = (uint64_t)O * Cc * R * S;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t s = i % S;
+        uint64_t t = i / S;
+        const uint32_t r = t % R;
+        t /= R;
+        const uint32_t c = t % Cc;
+        const uint32_t o = t / Cc;
+        out[i] = w[off + o * so + c * sc + r * sr + s * ss];
+    }
+}
+
+// Space-to-depth for a convolution whose windows tile the input exactly
+// (stride = kernel size, no padding, no dilation): row m = (n, p, q) of the
+// GEMM operand holds the window's C * kh * kw inputs in (c, r, s) order, so
+// the convolution is one dense [M, K] x [K, O] contraction.  Consecutive
+// threads walk s, i.e. consecutive input columns: reads and writes coalesce.
+template <typename E>
+__global__ void patches_kernel(const E* x, uint64_t off, uint64_t sn, uint64_t sc, uint64_t sh, uint64_t sw, uint32_t Cc,
+                               uint32_t R, uint32_t S, uint32_t P, uint32_t Q, uint64_t M, E* out) {
+    const uint64_t K = (uint64_t)Cc * R * S;
+    const uint64_t total = M * K;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t m = i / K, k = i % K;
+        const uint32_t s = (uint32_t)(k % S);
+        const uint32_t r = (uint32_t)((k / S) % R);
+        const uint32_t c = (uint32_t)(k / ((uint64_t)S * R));
+        const uint32_t q = (uint32_t)(m % Q);
+        const uint32_t pp = (uint32_t)((m / Q) % P);
+        const uint64_t n = m / ((uint64_t)Q * P);
+        out[i] = x[off + n * sn + c * sc + ((uint64_t)pp * R + r) * sh + ((uint64_t)q * S + s) * sw];
+    }
+}
+
 template <int BN>
 int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams& p, cudaStream_t st) {
     using C = Cfg<BN>;
@@ -327,13 +401,98 @@ uint32_t read_gemm_status() {
     return v;
 }
 
+// Channels-contiguous output whose rows start on 16-byte boundaries: the
+// epilogue may store each row's 32-column chunks as float4.
+bool c_rows_ok(const ConvArgs& a) {
+    if (a.out_stride_c != 1) return false;
+    const uint64_t strides[3] = {a.out_stride_n, a.out_strides[0], a.out_strides[1]};
+    for (uint64_t st : strides)
+        if (st % 4 != 0) return false;
+    return (reinterpret_cast<uintptr_t>(a.output + a.out_offset) % 16) == 0;
+}
+
+int launch_patches(const ConvArgs& a, void* stream) {
+    const uint64_t C = a.channels_per_group, R = a.k_dims[0], S = a.k_dims[1], O = a.out_channels;
+    const uint64_t P = a.out_dims[0], Q = a.out_dims[1], N = a.batch;
+    const uint64_t K = C * R * S, M = N * P * Q;
+    if (K % BK != 0 || M == 0 || M > 0x7fffffffull || M * K > (1ull << 40)) return FB_ERR_UNSUPPORTED;
+    const int BN = O % 256 == 0 ? 256 : O % 128 == 0 ? 128 : O % 64 == 0 ? 64 : 0;
+    if (BN == 0) return FB_ERR_UNSUPPORTED;
+    const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // A operand: gathered windows.
+    void* pa = scratch(stream, M * K * 2 + 256, SCRATCH_CONV_PATCH);
+    if (!pa) return FB_ERR_DRIVER;
+    {
+        const uint64_t total = M * K;
+        const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
+        patches_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.input), a.in_offset, a.in_stride_n,
+                                                        a.in_stride_c, a.in_strides[0], a.in_strides[1], (uint32_t)C,
+                                                        (uint32_t)R, (uint32_t)S, (uint32_t)P, (uint32_t)Q, M,
+                                                        static_cast<uint16_t*>(pa));
+        count_launch();
+        if (cudaGetLastError() != cudaSuccess) return launch_status("patch gather");
+    }
+    // B operand: [O, C, kh, kw] rows, in place when the weights are stored so.
+    const void* wptr = static_cast<const uint16_t*>(a.weight) + a.w_offset;
+    const bool oihw = a.w_stride_o == K && a.w_stride_c == R * S && a.w_strides[0] == S && a.w_strides[1] == 1 &&
+                      reinterpret_cast<uintptr_t>(wptr) % 16 == 0;
+    if (!oihw) {
+        void* tmp = scratch(stream, O * K * 2 + 256, SCRATCH_CONV_WEIGHT);
+        if (!tmp) return FB_ERR_DRIVER;
+        const uint64_t total = O * K;
+        const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 8);
+        weights_to_oihw_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.weight), a.w_offset,
+                                                               a.w_stride_o, a.w_stride_c, a.w_strides[0], a.w_strides[1],
+                                                               (uint32_t)O, (uint32_t)C, (uint32_t)R, (uint32_t)S,
+                                                               static_cast<uint16_t*>(tmp));
+        count_launch();
+        if (cudaGetLastError() != cudaSuccess) return launch_status("weight gather");
+        wptr = tmp;
+    }
+    CUtensorMap ta, tb;
+    if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN) || !make_2d_map(&ta, pa, fmt, K, M, K, BM))
+        return FB_ERR_UNSUPPORTED;
+    ConvGemmParams p{};
+    p.mode = 0;
+    p.fmt = fmt;
+    p.M = (uint32_t)M;
+    p.P = (uint32_t)P;
+    p.Q = (uint32_t)Q;
+    p.c_blocks = (uint32_t)(K / BK);
+    p.k_blocks = (uint32_t)(K / BK);
+    p.S = 1;
+    p.stride_h = p.stride_w = p.dil_h = p.dil_w = 1;
+    p.m_tiles = (uint32_t)((M + BM - 1) / BM);
+    p.n_tiles = (uint32_t)(O / BN);
+    p.out = a.output;
+    p.out_offset = a.out_offset;
+    p.s_n = a.out_stride_n;
+    p.s_c = a.out_stride_c;
+    p.s_p = a.out_strides[0];
+    p.s_q = a.out_strides[1];
+    p.c_rows = c_rows_ok(a) ? 1 : 0;
+    switch (BN) {
+        case 256: return launch_bn<256>(ta, tb, p, st);
+        case 128: return launch_bn<128>(ta, tb, p, st);
+        default: return launch_bn<64>(ta, tb, p, st);
+    }
+}
+
 int launch_conv_tc(const ConvArgs& a, void* stream) {
     if (a.dtype != FB_BF16 && a.dtype != FB_F16) return FB_ERR_UNSUPPORTED;
     if (a.spatial != 2 || a.outputs_per_group != a.out_channels) return FB_ERR_UNSUPPORTED;  // 2-D, one group
     const uint64_t C = a.channels_per_group, H = a.in_dims[0], W = a.in_dims[1];
     const uint64_t R = a.k_dims[0], S = a.k_dims[1], O = a.out_channels;
     const uint64_t P = a.out_dims[0], Q = a.out_dims[1], N = a.batch;
-    if (C % BK != 0 || O % 16 != 0 || O == 0) return FB_ERR_UNSUPPORTED;
+    if (O % 16 != 0 || O == 0) return FB_ERR_UNSUPPORTED;
+    // Windows that tile the input exactly (a ViT patch embedding) go through
+    // a space-to-depth gather and one dense GEMM, whatever the channel count.
+    // (trailing padding is never reached when P * R == H and Q * S == W)
+    const bool patches = a.stride[0] == R && a.stride[1] == S && a.pad[0] == 0 && a.pad[1] == 0 &&
+                         a.dilation[0] == 1 && a.dilation[1] == 1 && (R > 1 || S > 1) && P * R == H && Q * S == W;
+    if (patches) return launch_patches(a, stream);
+    if (C % BK != 0) return FB_ERR_UNSUPPORTED;
     // Channels-last input: c stride 1, w stride C, h stride W*C, n stride H*W*C.
     if (a.in_stride_c != 1 || a.in_strides[1] != C || a.in_strides[0] != W * C || a.in_stride_n != H * W * C)
         return FB_ERR_UNSUPPORTED;
@@ -361,8 +520,9 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     // B operand: dense [O, R*S*C] rows; gather when the weights are not OHWI.
     const uint64_t K = R * S * C;
     const void* wptr = static_cast<const uint16_t*>(a.weight) + a.w_offset;
-    const bool ohwi = a.w_stride_c == 1 && a.w_strides[1] == C && a.w_strides[0] == S * C && a.w_stride_o == K &&
-                      reinterpret_cast<uintptr_t>(wptr) % 16 == 0;
+    // (strides of unit kernel dimensions do not matter: [O, C, 1, 1] weights are dense rows)
+    const bool ohwi = a.w_stride_c == 1 && (S == 1 || a.w_strides[1] == C) && (R == 1 || a.w_strides[0] == S * C) &&
+                      a.w_stride_o == K && reinterpret_cast<uintptr_t>(wptr) % 16 == 0;
     if (!ohwi) {
         void* tmp = scratch(stream, O * K * 2 + 256, SCRATCH_CONV_WEIGHT);
         if (!tmp) return FB_ERR_DRIVER;
@@ -413,6 +573,7 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.s_c = a.out_stride_c;
     p.s_p = a.out_strides[0];
     p.s_q = a.out_strides[1];
+    p.c_rows = c_rows_ok(a) ? 1 : 0;
     switch (BN) {
         case 256: return launch_bn<256>(ta, tb, p, st);
         case 128: return launch_bn<128>(ta, tb, p, st);

@@ -82,6 +82,10 @@ __device__ __forceinline__ uint16_t encode_bf16(float value) {
     return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
 }
 __device__ __forceinline__ uint16_t encode_f16(float value) { return __half_as_ushort(__float2half_rn(value)); }
+__device__ __forceinline__ uint32_t encode_low_pair(float lo, float hi, uint32_t dtype) {
+    return dtype == FB_BF16 ? (uint32_t)encode_bf16(lo) | ((uint32_t)encode_bf16(hi) << 16)
+                            : (uint32_t)encode_f16(lo) | ((uint32_t)encode_f16(hi) << 16);
+}
 
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll

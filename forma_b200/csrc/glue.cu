@@ -1,0 +1,107 @@
+// Elementwise glue between the hot-path operators, for composite workloads
+// (an encoder forward that chains convolution, layer norm and attention needs
+// residual additions and an activation between them).
+//
+//   add          out = a + b in f32, operands with arbitrary strides (stride 0
+//                broadcasts), as the reference's `binary` kernel with its add
+//                op (compute-cuda/src/kernels.cu:29-58).
+//   gelu_to_low  the tanh form of GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x +
+//                0.044715 x^3))), as the reference's host activation
+//                (tensor-core/src/host_tensor/activation.rs:9-20), evaluated in
+//                f32 (in the equivalent form x / (1 + exp(-2u)), which does not
+//                cancel for negative x) and rounded once to f16/bf16 (round to nearest even, as
+//                encode_low in compute-cuda/src/low_precision.cu:6-16), so the
+//                activation feeds the next tensor-core contraction directly.
+// Both are memory-bound; the destination is contiguous and written once.
+#include <cuda_runtime.h>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace fb {
+namespace {
+
+constexpr int BLOCK = 256;
+
+__global__ void add_kernel(const float* a, uint64_t a_off, Nest an, const float* b, uint64_t b_off, Nest bn, float* out,
+                           uint64_t out_off, Nest on, uint64_t count) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+        out[out_off + nest_offset(on, i)] = __fadd_rn(a[a_off + nest_offset(an, i)], b[b_off + nest_offset(bn, i)]);
+}
+
+// Both operands dense and the same shape: four elements per thread.
+__global__ void add_dense_kernel(const float4* a, const float4* b, float4* out, uint64_t count4) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count4; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float4 x = a[i], y = b[i];
+        out[i] = make_float4(__fadd_rn(x.x, y.x), __fadd_rn(x.y, y.y), __fadd_rn(x.z, y.z), __fadd_rn(x.w, y.w));
+    }
+}
+
+// 0.5 x (1 + tanh(u)) evaluated as x / (1 + exp(-2u)), the same function:
+// the sum 1 + tanh(u) cancels catastrophically in f32 for u below about -4,
+// the quotient keeps full relative precision (and is exactly -0 once exp
+// overflows, where the f64 form also rounds to zero).
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    const float u = k0 * fmaf(k1 * x, x * x, x);
+    return x / (1.0f + expf(-2.0f * u));
+}
+
+__global__ void gelu_to_low_kernel(const float* in, uint64_t in_off, Nest n, uint16_t* out, uint32_t dtype,
+                                   uint64_t count) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float g = gelu_tanh(in[in_off + nest_offset(n, i)]);
+        out[i] = dtype == FB_BF16 ? encode_bf16(g) : encode_f16(g);
+    }
+}
+
+__global__ void gelu_to_low_vec8_kernel(const float* in, uint64_t in_off, Nest n, uint16_t* out, uint32_t dtype,
+                                        uint64_t runs) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < runs; t += (uint64_t)gridDim.x * blockDim.x) {
+        const float4* src = reinterpret_cast<const float4*>(in + in_off + nest_offset(n, t * 8));
+        const float4 a = src[0], b = src[1];
+        reinterpret_cast<uint4*>(out)[t] =
+            make_uint4(encode_low_pair(gelu_tanh(a.x), gelu_tanh(a.y), dtype), encode_low_pair(gelu_tanh(a.z), gelu_tanh(a.w), dtype),
+                       encode_low_pair(gelu_tanh(b.x), gelu_tanh(b.y), dtype), encode_low_pair(gelu_tanh(b.z), gelu_tanh(b.w), dtype));
+    }
+}
+
+unsigned grid_of(uint64_t work) {
+    const uint64_t cap = (uint64_t)sm_count() * 16;
+    const uint64_t blocks = (work + BLOCK - 1) / BLOCK;
+    return (unsigned)(blocks == 0 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+}  // namespace
+
+int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, uint64_t b_off, const Nest& bn, float* out,
+               uint64_t out_off, const Nest& on, uint64_t count, bool dense, void* stream) {
+    if (count == 0) return FB_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (dense) {
+        add_dense_kernel<<<grid_of(count / 4), BLOCK, 0, st>>>(reinterpret_cast<const float4*>(a + a_off),
+                                                              reinterpret_cast<const float4*>(b + b_off),
+                                                              reinterpret_cast<float4*>(out + out_off), count / 4);
+    } else {
+        add_kernel<<<grid_of(count), BLOCK, 0, st>>>(a, a_off, an, b, b_off, bn, out, out_off, on, count);
+    }
+    count_launch();
+    return launch_status("add");
+}
+
+int launch_gelu_to_low(const float* in, uint64_t in_off, const Nest& n, uint16_t* out, uint32_t dtype, uint64_t count,
+                       void* stream) {
+    if (count == 0) return FB_OK;
+    if (vec8_ok(n, in, in_off, out)) {
+        const uint64_t runs = count / 8;
+        gelu_to_low_vec8_kernel<<<grid_of(runs), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(in, in_off, n, out, dtype,
+                                                                                                 runs);
+    } else {
+        gelu_to_low_kernel<<<grid_of(count), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(in, in_off, n, out, dtype,
+                                                                                            count);
+    }
+    count_launch();
+    return launch_status("gelu");
+}
+
+}  // namespace fb

@@ -74,8 +74,9 @@ enum StatsOp : uint32_t {
 enum ScratchSlot : int {
     SCRATCH_SUM = 0,          // global-sum block partials + finishing counter
     SCRATCH_CONV_RESULT = 1,  // f32 convolution result before low rounding
-    SCRATCH_CONV_WEIGHT = 2,  // weights gathered into [O, kh, kw, C]
-    SCRATCH_SLOTS = 3,
+    SCRATCH_CONV_WEIGHT = 2,  // weights gathered into [O, kh, kw, C] or [O, C, kh, kw]
+    SCRATCH_CONV_PATCH = 3,   // non-overlapping patches gathered into [N*P*Q, C*kh*kw]
+    SCRATCH_SLOTS = 4,
 };
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
@@ -104,6 +105,22 @@ int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream);
 int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const Nest& in_nest, void* out,
                 uint64_t out_offset, const Nest& out_nest, uint64_t count, void* stream);
 // Rounds f32 (strided) into F16/BF16 contiguous storage, nearest-even.
+// An f32 -> 16-bit elementwise pass may move 8 elements per thread (two
+// float4 loads, one 16-byte store) when the nest's innermost axis is
+// contiguous with a multiple of 8 elements and every run starts 16-byte
+// aligned on both sides.
+inline bool vec8_ok(const Nest& n, const float* in, uint64_t in_offset, const uint16_t* out) {
+    if (n.rank == 0 || n.strides[n.rank - 1] != 1 || n.dims[n.rank - 1] % 8 != 0) return false;
+    for (uint32_t d = 0; d + 1 < n.rank; ++d)
+        if (n.strides[d] % 4 != 0) return false;
+    return reinterpret_cast<uintptr_t>(in + in_offset) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+}
+
+// ---- elementwise glue (glue.cu) ----
+int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, uint64_t b_off, const Nest& bn, float* out,
+               uint64_t out_off, const Nest& on, uint64_t count, bool dense, void* stream);
+int launch_gelu_to_low(const float* in, uint64_t in_off, const Nest& n, uint16_t* out, uint32_t dtype, uint64_t count,
+                       void* stream);
 int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest, uint16_t* out, uint32_t dtype,
                        uint64_t count, void* stream);
 

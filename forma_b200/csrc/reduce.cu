@@ -574,6 +574,16 @@ __global__ void cast_to_low_kernel(const float* in, uint64_t in_offset, Nest in_
     }
 }
 
+__global__ void cast_to_low_vec8_kernel(const float* in, uint64_t in_offset, Nest in_nest, uint16_t* out, uint32_t dtype,
+                                        uint64_t runs) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < runs; t += (uint64_t)gridDim.x * blockDim.x) {
+        const float4* src = reinterpret_cast<const float4*>(in + in_offset + nest_offset(in_nest, t * 8));
+        const float4 a = src[0], b = src[1];
+        reinterpret_cast<uint4*>(out)[t] = make_uint4(encode_low_pair(a.x, a.y, dtype), encode_low_pair(a.z, a.w, dtype),
+                                                      encode_low_pair(b.x, b.y, dtype), encode_low_pair(b.z, b.w, dtype));
+    }
+}
+
 unsigned grid_for(uint64_t work, unsigned per_sm = 8) {
     const uint64_t cap = (uint64_t)sm_count() * per_sm;
     uint64_t g = work < cap ? work : cap;
@@ -819,6 +829,12 @@ int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const N
 int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest, uint16_t* out, uint32_t dtype,
                        uint64_t count, void* stream) {
     if (count == 0) return FB_OK;
+    if (vec8_ok(in_nest, in, in_offset, out)) {
+        const uint64_t runs = count / 8;
+        cast_to_low_vec8_kernel<<<grid_for((runs + BLOCK - 1) / BLOCK, 16), BLOCK, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(in, in_offset, in_nest, out, dtype, runs);
+        return check_launch();
+    }
     cast_to_low_kernel<<<grid_for((count + BLOCK - 1) / BLOCK), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(
         in, in_offset, in_nest, out, dtype, count);
     return check_launch();

@@ -1,0 +1,164 @@
+"""A ViT-style encoder forward chained from the operator API.
+
+The composite workload that exercises the three hot-path families together:
+convolution (the patch embedding and the token projections as 1x1
+convolutions on a channels-last token map), layer norm, and fused attention,
+joined by residual additions and a GELU.  Pre-norm blocks::
+
+    x  = [cls; patches(img) W_p] + pos                 conv 16x16 stride 16
+    for each layer:
+        h  = LN(x)                                     layer_norm, eps 1e-5
+        q, k, v = heads(h W_qkv)                       1x1 conv, cast per head
+        x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv
+        h  = LN(x)
+        x  = x + GELU(h W_1) W_2                        1x1 convs
+
+Tokens live as a channels-last [B, 1, L, E] map, so every projection is a
+1x1 convolution whose input rows are the tokens (the tensor-core implicit
+GEMM reads them in place) and whose f32 result is written channels-last
+through a permuted output view.  Operands of the contractions are rounded
+to the low dtype at the points marked by the casts; everything else is f32.
+Weights are random (seeded); no checkpoint is involved.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import api
+from .api import AttentionOptions, ConvOptions
+
+
+@dataclass(frozen=True)
+class ViTConfig:
+    batch: int = 64
+    image: int = 224
+    channels: int = 3
+    patch: int = 16
+    embed: int = 768
+    heads: int = 12
+    layers: int = 12
+    mlp: int = 3072
+    eps: float = 1e-5
+
+    @property
+    def grid(self) -> int:
+        return self.image // self.patch
+
+    @property
+    def tokens(self) -> int:
+        return self.grid * self.grid + 1
+
+    @property
+    def head_dim(self) -> int:
+        return self.embed // self.heads
+
+    def flops(self) -> dict:
+        """Multiply-add FLOPs (2 per MAC) of each stage of one forward."""
+        B, L, E, M = self.batch, self.tokens, self.embed, self.mlp
+        P = self.grid * self.grid
+        K = self.channels * self.patch * self.patch
+        per_layer = {
+            "qkv": 2 * B * L * E * 3 * E,
+            "attention": 4 * B * self.heads * L * L * self.head_dim,
+            "proj": 2 * B * L * E * E,
+            "mlp": 2 * 2 * B * L * E * M,
+        }
+        out = {"patch": 2 * B * P * E * K}
+        for k, v in per_layer.items():
+            out[k] = v * self.layers
+        out["total"] = sum(out.values())
+        return out
+
+
+class ViTEncoder:
+    """Random-init encoder; ``forward(img)`` takes [B, C, H, W] in the low dtype
+    and returns the final tokens [B, L, E] (f32)."""
+
+    def __init__(self, cfg: ViTConfig, device, dtype=torch.bfloat16, seed: int = 0):
+        self.cfg, self.dtype, self.device = cfg, dtype, torch.device(device)
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        E, M, K = cfg.embed, cfg.mlp, cfg.channels * cfg.patch * cfg.patch
+
+        def w(o, i, kh=1, kw=1, fan=None):
+            t = torch.randn(o, i, kh, kw, generator=g) / math.sqrt(fan or i * kh * kw)
+            return t.to(dtype).to(self.device)
+
+        self.w_patch = w(E, cfg.channels, cfg.patch, cfg.patch, fan=K)
+        self.cls = (torch.randn(1, 1, E, generator=g) * 0.02).to(self.device)
+        self.pos = (torch.randn(1, cfg.tokens, E, generator=g) * 0.02).to(self.device)
+        self.blocks = []
+        for _ in range(cfg.layers):
+            self.blocks.append({
+                "qkv": w(3 * E, E),
+                "proj": w(E, E),
+                "fc1": w(M, E),
+                "fc2": w(E, M),
+            })
+        self._bufs = None
+
+    def _buffers(self, B: int):
+        if self._bufs is not None and self._bufs["B"] == B:
+            return self._bufs
+        cfg, dev, low = self.cfg, self.device, self.dtype
+        L, E, M, H, D = cfg.tokens, cfg.embed, cfg.mlp, cfg.heads, cfg.head_dim
+        G = cfg.grid
+        self._bufs = {
+            "B": B,
+            "x": torch.empty(B, L, E, device=dev),
+            "patches": torch.empty(B, G, G, E, device=dev),      # channels-last conv result
+            "h_low": torch.empty(B, L, E, dtype=low, device=dev),
+            "qkv": torch.empty(B, 1, L, 3 * E, device=dev),
+            "q": torch.empty(B, H, L, D, dtype=low, device=dev),
+            "k": torch.empty(B, H, L, D, dtype=low, device=dev),
+            "v": torch.empty(B, H, L, D, dtype=low, device=dev),
+            "a_low": torch.empty(B, L, E, dtype=low, device=dev),
+            "o": torch.empty(B, 1, L, E, device=dev),
+            "m": torch.empty(B, 1, L, M, device=dev),
+            "m_low": torch.empty(B, 1, L, M, dtype=low, device=dev),
+        }
+        return self._bufs
+
+    @staticmethod
+    def _proj(x_low: torch.Tensor, weight: torch.Tensor, out: torch.Tensor) -> None:
+        """1x1 convolution of channels-last tokens [B, L, Cin] into out [B, 1, L, Cout] (f32)."""
+        B, L, Cin = x_low.shape
+        xin = x_low.view(B, 1, L, Cin).permute(0, 3, 1, 2)  # logical [B, Cin, 1, L], channels-last storage
+        api.conv_low_f32_into(xin, weight, ConvOptions([1, 1], [1, 1], [0, 0], [0, 0]), out.permute(0, 3, 1, 2))
+
+    def forward(self, img: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        B = img.shape[0]
+        L, E, H, D, M = cfg.tokens, cfg.embed, cfg.heads, cfg.head_dim, cfg.mlp
+        b = self._buffers(B)
+        x = b["x"]
+        # patch embedding (space-to-depth + tensor-core GEMM), then [cls; patches] + pos
+        p = cfg.patch
+        api.conv_low_f32_into(img, self.w_patch, ConvOptions([p, p], [1, 1], [0, 0], [0, 0]),
+                              b["patches"].permute(0, 3, 1, 2))
+        api.add(b["patches"].view(B, L - 1, E), self.pos[:, 1:].expand(B, L - 1, E), out=x[:, 1:])
+        api.add(self.cls.expand(B, 1, E), self.pos[:, :1].expand(B, 1, E), out=x[:, :1])
+        opts = AttentionOptions()  # default scale 1/sqrt(D), non-causal
+        for blk in self.blocks:
+            # attention sub-block
+            h = api.layer_norm(x, [2], cfg.eps)
+            api.cast_to_low_into(h, b["h_low"])
+            self._proj(b["h_low"], blk["qkv"], b["qkv"])
+            qkv = b["qkv"].view(B, L, 3, H, D)
+            for i, name in enumerate(("q", "k", "v")):
+                api.cast_to_low_into(qkv[:, :, i].permute(0, 2, 1, 3), b[name])
+            a = api.attention_low_f32(b["q"], b["k"], b["v"], None, opts)
+            api.cast_to_low_into(a.permute(0, 2, 1, 3), b["a_low"].view(B, L, H, D))
+            self._proj(b["a_low"], blk["proj"], b["o"])
+            api.add(x, b["o"].view(B, L, E), out=x)
+            # MLP sub-block
+            h = api.layer_norm(x, [2], cfg.eps)
+            api.cast_to_low_into(h, b["h_low"])
+            self._proj(b["h_low"], blk["fc1"], b["m"])
+            api.gelu_to_low(b["m"], self.dtype, out=b["m_low"])
+            self._proj(b["m_low"].view(B, L, M), blk["fc2"], b["o"])
+            api.add(x, b["o"].view(B, L, E), out=x)
+        return x

@@ -287,6 +287,25 @@ int fb_layer_norm(const fb_tensor* input, const uint32_t* axes,
  * F16/BF16 of `output->dtype`; `output` must be contiguous. */
 int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream);
 
+/* ------------------------------------------------------- elementwise glue */
+
+/* Glue for composite workloads that chain the operators above (residual
+ * additions, the activation between two contractions).  Not part of the
+ * reference's conv/attention/reduction path; the arithmetic follows the
+ * reference's own elementwise definitions.
+ *
+ * out = a + b in f32, the `binary` kernel with its add op
+ * (compute-cuda/src/kernels.cu:29-58).  `a` and `b` have `output`'s dims and
+ * any strides (0 broadcasts); `output` may have any layout that addresses each
+ * element once, and an operand may share memory with it only as the
+ * identical view (an in-place update). */
+int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stream);
+
+/* tanh-form GELU (tensor-core/src/host_tensor/activation.rs:9-20) of an f32
+ * input, rounded once to `output->dtype` (F16/BF16, nearest even); `output`
+ * is contiguous with `input`'s dims. */
+int fb_gelu_to_low(const fb_tensor* input, fb_tensor* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

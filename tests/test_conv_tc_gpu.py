@@ -65,6 +65,13 @@ def test_tc_conv_oihw_weights_and_nhwc_output(cuda):
     run_case(cuda, 2, 14, 14, 256, 128, 3, pad=1, ohwi=False, nchw_out=False)
 
 
+def test_tc_conv_nhwc_output_partial_tile(cuda):
+    # channels-last f32 result through the staged float4 epilogue; M = 189
+    # leaves a partial last tile whose missing rows must not be stored
+    run_case(cuda, 3, 7, 9, 64, 64, 1, nchw_out=False)
+    run_case(cuda, 3, 7, 7, 512, 64, 3, pad=1, nchw_out=False)
+
+
 def test_tc_conv_f16(cuda):
     run_case(cuda, 2, 14, 14, 256, 256, 3, pad=1, dtype=torch.float16)
 

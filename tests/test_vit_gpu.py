@@ -1,0 +1,144 @@
+"""The encoder chain (patch conv -> layer norm -> attention -> projections ->
+GELU MLP, residual additions) against the oracle composed in the same order
+with the same low-precision rounding points, plus the pieces the chain adds:
+the space-to-depth patch convolution route and the elementwise glue."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from forma_b200 import api
+from forma_b200.api import ConvOptions
+from forma_b200.vit import ViTConfig, ViTEncoder
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def low(x):
+    """Nearest-even rounding to BF16 and back (the casts of the chain)."""
+    return orc.decode_bits(orc.round_bits(np.asarray(x, np.float32), "bf16"), "bf16").astype(np.float64)
+
+
+def gelu_tanh(x):
+    # tensor-core/src/host_tensor/activation.rs:9-20, in f64
+    return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+
+def f32(x):
+    return np.asarray(x, np.float64).astype(np.float32).astype(np.float64)
+
+
+def oracle_forward(enc: ViTEncoder, img: torch.Tensor) -> np.ndarray:
+    cfg = enc.cfg
+    B, L, E, H, D = img.shape[0], cfg.tokens, cfg.embed, cfg.heads, cfg.head_dim
+    w = lambda t: t.float().cpu().numpy().astype(np.float64)
+    p = cfg.patch
+    pt = orc.conv(w(img), w(enc.w_patch), [p, p], [1, 1], [0, 0], [0, 0], nthreads=orc.threads())
+    patches = f32(pt.reshape(B, E, -1).transpose(0, 2, 1))                     # [B, P, E] f32 conv result
+    pos, cls = w(enc.pos), w(enc.cls)
+    x = np.concatenate([np.broadcast_to(f32(cls + pos[:, :1]), (B, 1, E)), f32(patches + pos[:, 1:])], axis=1)
+
+    def norm(t):
+        return orc.row_stats(t.reshape(-1, E).astype(np.float32), cfg.eps, which=("norm",))["norm"].astype(
+            np.float64).reshape(t.shape)
+
+    def proj(t, weight):
+        return f32(t @ w(weight)[:, :, 0, 0].T)
+
+    for blk in enc.blocks:
+        h = low(norm(x))
+        qkv = proj(h, blk["qkv"]).reshape(B, L, 3, H, D)
+        q, k, v = (low(qkv[:, :, i].transpose(0, 2, 1, 3)) for i in range(3))
+        a = orc.attention(q, k, v, nthreads=orc.threads())
+        a_low = low(np.asarray(a, np.float64).transpose(0, 2, 1, 3).reshape(B, L, E))
+        x = f32(x + proj(a_low, blk["proj"]))
+        m = proj(low(norm(x)), blk["fc1"])
+        x = f32(x + proj(low(gelu_tanh(m)), blk["fc2"]))
+    return x
+
+
+def test_vit_chain_small_matches_oracle(cuda):
+    cfg = ViTConfig(batch=8, image=64, channels=3, patch=16, embed=128, heads=2, layers=2, mlp=256)
+    enc = ViTEncoder(cfg, cuda, seed=3)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    img = torch.randn(cfg.batch, cfg.channels, cfg.image, cfg.image, generator=g).bfloat16()
+    before = api.launch_count()
+    out = enc.forward(img.to(cuda)).cpu().numpy()
+    assert api.device_status() == 0
+    assert api.launch_count() > before
+    ref = oracle_forward(enc, img)
+    assert out.shape == ref.shape == (cfg.batch, cfg.tokens, cfg.embed)
+    assert np.isfinite(out).all()
+    err = float(np.abs(out - ref).max() / np.abs(ref).max())
+    assert err <= 2e-2, err  # bf16 tensor-core gate, applied to the chain's output
+
+
+def test_vit_flop_count_matches_configuration():
+    f = ViTConfig().flops()
+    assert f["patch"] == 14_797_504_512                  # 2 * 64 * 196 * 768 * 768
+    assert f["attention"] == 12 * 7_630_159_872          # 4 * B * H * L^2 * D per layer
+
+
+@pytest.mark.parametrize("contiguous_weights", [True, False])
+def test_patch_convolution_route(cuda, contiguous_weights):
+    g = torch.Generator(device="cpu").manual_seed(5)
+    x = torch.randn(4, 3, 64, 64, generator=g).bfloat16()
+    w = (torch.randn(256, 3, 16, 16, generator=g) / math.sqrt(768)).bfloat16()
+    wd = w.to(cuda)
+    if not contiguous_weights:
+        wd = wd.permute(0, 2, 3, 1).contiguous().permute(0, 3, 1, 2)  # OHWI storage, OIHW view
+    out = api.conv_low_f32(x.to(cuda), wd, ConvOptions([16, 16], [1, 1], [0, 0], [0, 0])).cpu().numpy()
+    ref = orc.conv(x.float().numpy(), w.float().numpy(), [16, 16], [1, 1], [0, 0], [0, 0])
+    err = float(np.abs(out - ref).max() / np.abs(ref).max())
+    assert err <= 2e-2, err
+    # f32 accumulation of exactly representable products: far tighter than the gate
+    assert err <= 1e-4, err
+
+
+def test_add_broadcast_and_strided_output(cuda):
+    g = torch.Generator(device="cpu").manual_seed(6)
+    a = torch.randn(3, 5, 7, generator=g)
+    bias = torch.randn(1, 5, 7, generator=g)
+    big = torch.zeros(3, 6, 7, device=cuda)
+    api.add(a.to(cuda), bias.to(cuda).expand(3, 5, 7), out=big[:, 1:])
+    got = big.cpu().numpy()
+    exp = (a.numpy() + bias.numpy()).astype(np.float32)
+    assert np.array_equal(got[:, 1:].view(np.uint32), exp.view(np.uint32))  # one f32 add, bit-exact
+    assert (got[:, 0] == 0).all()
+    # in place on the identical view
+    x = a.to(cuda).contiguous()
+    api.add(x, x, out=x)
+    assert np.array_equal(x.cpu().numpy(), (a.numpy() * 2).astype(np.float32))
+    with pytest.raises(api.TensorError):
+        api.add(big[:, :5], big[:, 1:], out=big[:, 1:])  # overlapping, not identical
+
+
+def test_gelu_to_low_matches_tanh_form(cuda):
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(4096, generator=g) * 4
+    got = api.gelu_to_low(x.to(cuda), torch.bfloat16).float().cpu().numpy().astype(np.float64)
+    exp = low(gelu_tanh(x.numpy().astype(np.float64)))
+    # f32 evaluation can move a value across a BF16 rounding boundary: one BF16
+    # step at most; below 1e-6 in magnitude the f64 form itself has no
+    # relative accuracy left (1 + tanh cancels), so compare absolutely there.
+    tol = np.abs(exp) * 2.0 ** -7 + 1e-6  # a BF16 step is at most 2^-7 of the value
+    assert (np.abs(got - exp) <= tol).all()
+    # where the f64 form keeps its precision (|GELU| above 1e-4), the BF16
+    # results agree bit for bit except for rare rounding-boundary cases
+    m = np.abs(exp) > 1e-4
+    assert (got[m] == exp[m]).mean() > 0.99
+
+
+@pytest.mark.parametrize("inner", [64, 13])
+def test_cast_to_low_strided_views(cuda, inner):
+    """Head-split views (innermost axis contiguous: 8-element vector path when
+    its length allows, element path otherwise), nearest-even BF16."""
+    g = torch.Generator(device="cpu").manual_seed(8)
+    x = torch.randn(2, 5, 3, 4, inner, generator=g)
+    view = x.to(cuda)[:, :, 1].permute(0, 2, 1, 3)  # [2, 4, 5, inner], strides not dense
+    got = api.cast_to_low(view, torch.bfloat16).float().cpu().numpy()
+    exp = low(x[:, :, 1].permute(0, 2, 1, 3).numpy())
+    assert np.array_equal(got, exp)
