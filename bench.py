@@ -593,6 +593,13 @@ def run_profile(args) -> int:
     elif name == "rows_moments":
         x = torch.randn(args.rows, COLS, device=dev, generator=g)
         fn = lambda: api.moments(x, [1])  # noqa: E731
+    elif name == "vit_c5":
+        from forma_b200.vit import ViTConfig, ViTEncoder
+
+        cfg = ViTConfig()
+        enc = ViTEncoder(cfg, dev)
+        img = torch.randn(cfg.batch, cfg.channels, cfg.image, cfg.image, device=dev, generator=g).bfloat16()
+        fn = lambda: enc.forward(img)  # noqa: E731
     else:
         raise SystemExit(f"unknown profile workload {name}")
     for _ in range(max(1, args.steps)):
@@ -616,7 +623,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end pass (profiling runs)")
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--profile", default=None,
-                    help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, "
+                    help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, vit_c5, "
                          "conv_c1, rows_softmax, rows_argmax, rows_moments)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "forma":

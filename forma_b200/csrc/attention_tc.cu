@@ -5,7 +5,8 @@
 // of one (batch, head) and streams that head's K/V once for both tiles.
 //   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys
 //               into a 2-stage ring (128B-swizzled boxes of 64 depth columns).
-//   warp 1      TMEM allocator and MMA issuer.  Per key tile j, per Q tile t:
+//   warp 1      TMEM allocator and MMA issuer (the whole warp runs the issue
+//               loop; one elected lane issues).  Per key tile j, per Q tile t:
 //                 S_t = Q_t K_j^T  -> TMEM S_t (128 x 128 f32)
 //                 O_t += P_t V_j   -> TMEM O_t (128 x D f32), P_t read from
 //                                     TMEM where it overwrote S_t (tcgen05.mma
@@ -18,9 +19,9 @@
 //               input extremes), one FFMA per score, exp2 (seven pairs in
 //               eight on MUFU ex2, one as a paired polynomial on the FMA pipe),
 //               paired running sums, P packed to 16-bit pairs with integer ops
-//               (BF16) and written back over S with tcgen05.st.  The running max is only
-//               raised (and O rescaled in TMEM) when a row max exceeds it
-//               by more than 2^8, so P <= 2^8 and rescales are rare.
+//               (BF16) and written back over S with tcgen05.st.  The running
+//               max is only raised (and O rescaled in TMEM) when a row max
+//               exceeds it by more than 2^8, so P <= 2^8 and rescales are rare.
 //               Finally O / l is written as f32.
 // Ordering: a tcgen05.commit completes only after every earlier MMA of the
 // issuing thread, so "S_t of tile j+1 ready" also certifies that PV_t of tile
@@ -263,35 +264,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
                 (void)mbar_wait(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
         }
         if (n_kv > 0) (void)mbar_wait(q_full, 0);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
+        // The whole warp runs this loop with warp-uniform operands and waits;
+        // one elected lane issues each tcgen05.mma / commit.  Descriptors are
+        // built once per group and advanced by constant byte offsets.
         const uint32_t idesc_s = f16_idesc(p.fmt, TQ, TK);
         const uint32_t idesc_o = f16_idesc(p.fmt, TQ, D) | (1u << 16);  // B (V) is MN-major
-        bool ok = n_kv == 0 || mbar_wait(q_full, 0);
+        auto wait = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
+        bool ok = n_kv == 0 || wait(q_full, 0);
         auto issue_s = [&](int t, uint32_t j) -> bool {
             const uint32_t s = j % C::STAGES;
-            if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1)) return false;
+            if (!wait(&kv_full[s], (j / C::STAGES) & 1)) return false;
             tc_fence_after();
-            const uint32_t q_addr = smem_u32(sQ + t * C::Q_BYTES);
-            const uint32_t k_addr = smem_u32(sKV + s * C::STAGE_BYTES);
+            const uint64_t qd = sw128_desc(smem_u32(sQ + t * C::Q_BYTES));
+            const uint64_t kd = sw128_desc(smem_u32(sKV + s * C::STAGE_BYTES));
+            const uint32_t d = tmem + C::s_col(t);
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
                 const uint32_t off = (uint32_t)((k / 4) * (TQ * 128) + (k % 4) * 32);
-                umma_f16_ss(tmem + C::s_col(t), sw128_desc(q_addr + off), sw128_desc(k_addr + off), idesc_s, k != 0);
+                umma_f16_ss_warp(d, desc_add(qd, off), desc_add(kd, off), idesc_s, k != 0);
             }
-            umma_commit(&s_full[t]);
+            umma_commit_warp(&s_full[t]);
             return true;
         };
         auto issue_pv = [&](int t, uint32_t j) -> bool {
             const uint32_t s = j % C::STAGES;
-            if (!mbar_wait(&p_full[t], j & 1)) return false;
+            if (!wait(&p_full[t], j & 1)) return false;
             tc_fence_after();
-            const uint32_t v_addr = smem_u32(sKV + s * C::STAGE_BYTES + C::K_BYTES);
+            const uint64_t vd = sw128_mn_desc(smem_u32(sKV + s * C::STAGE_BYTES + C::K_BYTES), TK * 128);
+            const uint32_t d = tmem + C::o_col(t), a = tmem + C::s_col(t);
+            umma_f16_ts_warp(d, a, vd, idesc_o, j != 0);
 #pragma unroll
-            for (int k = 0; k < TK / 16; ++k)
-                umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + k * 8, sw128_mn_desc(v_addr + k * 16 * 128, TK * 128),
-                            idesc_o, (j | k) != 0);
-            if (j + 1 == n_t[t]) umma_commit(&o_done[t]);
+            for (int k = 1; k < TK / 16; ++k) umma_f16_ts_warp(d, a + k * 8, desc_add(vd, k * 16 * 128), idesc_o, 1u);
+            if (j + 1 == n_t[t]) umma_commit_warp(&o_done[t]);
             return true;
         };
         for (int t = 0; t < QT && ok; ++t)
@@ -303,11 +309,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
                 if (ok && j + 1 < n_t[t]) ok = issue_s(t, j + 1);
             }
             // stage j is free once every PV reading it has completed
-            if (ok) umma_commit(&kv_empty[j % C::STAGES]);
+            if (ok) umma_commit_warp(&kv_empty[j % C::STAGES]);
         }
-        if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
-        umma_commit(drain);
-        (void)mbar_wait(drain, 0);
+        if (!ok && lane == 0) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+        umma_commit_warp(drain);
+        (void)wait(drain, 0);
     } else if (warp >= 2) {
         // ------------------------------------------------ softmax / epilogue
         const int t = (warp - 2) / 4;                  // Q tile of this warpgroup

@@ -13,7 +13,8 @@
 //      one tile overlaps the main loop of the next.
 // Warp roles in a 192-thread CTA, persistent over output tiles:
 //   warp 0      TMA producer (one lane) into a STAGES-deep smem ring
-//   warp 1      TMEM allocator and MMA issuer (one lane)
+//   warp 1      TMEM allocator and MMA issuer (the warp runs the issue loop,
+//               one elected lane issues each MMA)
 //   warps 2-5   epilogue: tcgen05.ld -> f32 stores at the output's strides
 // Every wait is bounded (async.cuh); a timeout sets a status bit and the CTA
 // drains its copies and MMAs before releasing TMEM and exiting.
@@ -152,46 +153,49 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                 (void)mbar_wait(&full[s], ph);
             }
         }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
+        // The whole warp runs the loop with warp-uniform operands and waits;
+        // one elected lane issues each tcgen05.mma / commit.
         const uint32_t idesc = f16_idesc(p.fmt, BM, BN);
+        auto wait = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
         uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
         bool failed = false;
         for (uint32_t t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
-            if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+            if (!wait(&tempty[acc], acc_phase ^ 1)) {
                 failed = true;
                 break;
             }
             tc_fence_after();
             const uint32_t d = tmem + acc * BN;
             for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
-                if (!mbar_wait(&full[stage], phase)) {
+                if (!wait(&full[stage], phase)) {
                     failed = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(ring + stage * C::STAGE_BYTES);
-                const uint32_t b_addr = a_addr + C::A_BYTES;
+                const uint64_t ad = sw128_desc(smem_u32(ring + stage * C::STAGE_BYTES));
+                const uint64_t bd = desc_add(ad, C::A_BYTES);
+                umma_f16_ss_warp(d, ad, bd, idesc, kb != 0);
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)
-                    umma_f16_ss(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
-                umma_commit(&empty[stage]);  // frees the stage when these MMAs complete
+                for (int k = 1; k < BK / 16; ++k) umma_f16_ss_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 32), idesc, 1u);
+                umma_commit_warp(&empty[stage]);  // frees the stage when these MMAs complete
                 if (++stage == C::STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
             if (failed) break;
-            umma_commit(&tfull[acc]);  // accumulator complete
+            umma_commit_warp(&tfull[acc]);  // accumulator complete
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
-        if (failed) atomicOr(&g_gemm_status, 1u << DEV_GEMM_MMA_TIMEOUT);
-        // All MMAs issued by this thread have finished once `drain` completes.
-        umma_commit(drain);
-        (void)mbar_wait(drain, 0);
+        if (failed && lane == 0) atomicOr(&g_gemm_status, 1u << DEV_GEMM_MMA_TIMEOUT);
+        // All MMAs issued by this warp have finished once `drain` completes.
+        umma_commit_warp(drain);
+        (void)wait(drain, 0);
     } else if (warp >= 2) {
         // ------------------------------------------------ epilogue
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, +32)
