@@ -593,6 +593,13 @@ def run_profile(args) -> int:
     elif name == "rows_moments":
         x = torch.randn(args.rows, COLS, device=dev, generator=g)
         fn = lambda: api.moments(x, [1])  # noqa: E731
+    elif name == "rows_max_argmax_moments":
+        x = torch.randn(args.rows, COLS, device=dev, generator=g)
+
+        def fn():
+            api.reduce_f32(ReduceOp.Max, x, [1])
+            api.argmax(x, 1)
+            api.moments(x, [1])
     elif name == "vit_c5":
         from forma_b200.vit import ViTConfig, ViTEncoder
 
@@ -624,6 +631,7 @@ def main(argv=None) -> int:
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--profile", default=None,
                     help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, vit_c5, "
+                         "rows_max_argmax_moments, "
                          "conv_c1, rows_softmax, rows_argmax, rows_moments)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "forma":

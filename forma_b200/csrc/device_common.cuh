@@ -67,6 +67,18 @@ struct Elem<__half> {
 
 // Total-order key of an f32 (reduce_float_key, compute-cuda/src/reductions.cu:
 // 31-34): unsigned comparison of keys orders -0 < +0 and preserves bits.
+// Three-input min/max that propagate NaN (sm_100 forms).
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float min3_nan(float a, float b, float c) {
+    float d;
+    asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t order_key(float x) {
     const uint32_t b = __float_as_uint(x);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);

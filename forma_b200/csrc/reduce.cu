@@ -284,8 +284,8 @@ __device__ __forceinline__ float4 smem_load4(const unsigned char* row, uint64_t 
 // Operation codes of the streamed engine: RowOp values, then StatsOp + 16.
 constexpr uint32_t STREAM_STATS = 16;
 
-template <typename T, int NV>
-__global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
+template <typename T, int NV, int TB>
+__global__ void __launch_bounds__(TB) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
                                                             float eps, uint32_t stages, uint32_t row_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -293,9 +293,10 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
     // Per-warp partials, double-buffered by row parity so that one barrier per
     // block reduction suffices (a row's partials are never overwritten before
     // every thread has passed the next row's first barrier).
-    __shared__ double s_d[2][2][BLOCK / 32];
-    __shared__ float s_f[2][BLOCK / 32];
-    __shared__ uint64_t s_k[2][BLOCK / 32];
+    __shared__ double s_d[2][2][TB / 32];
+    __shared__ double s_a[2][TB / 32];  // moments: sums of |x| (error bound of the f32 pass)
+    __shared__ float s_f[2][TB / 32];
+    __shared__ uint64_t s_k[2][TB / 32];
     __shared__ int s_abort;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint64_t first = blockIdx.x, step = gridDim.x;
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
         const unsigned char* rb = ring + (uint64_t)s * row_bytes;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const uint64_t v = tid + (uint64_t)j * BLOCK;
+            const uint64_t v = tid + (uint64_t)j * TB;
             c[j] = v * 4 < n ? smem_load4<T>(rb, v) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         const uint64_t row = first + i * step;
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             __syncthreads();
             if (tid == 0 && i + stages < mine && !s_abort) issue(i + stages);
         };
-        auto valid = [&](int j) { return (tid + (uint64_t)j * BLOCK) * 4 < n; };
+        auto valid = [&](int j) { return (tid + (uint64_t)j * TB) * 4 < n; };
 
         if (op == ROW_SUM || op == ROW_MEAN) {
             double a = 0.0;
@@ -351,7 +352,7 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             if (tid == 0) {
                 double t = 0.0;
 #pragma unroll
-                for (int w = 0; w < BLOCK / 32; ++w) t += s_d[0][par][w];
+                for (int w = 0; w < TB / 32; ++w) t += s_d[0][par][w];
                 static_cast<float*>(oa.data)[out_index(oa, row)] = op == ROW_MEAN ? (float)(t / (double)n) : (float)t;
             }
         } else if (op == ROW_MIN || op == ROW_MAX || op == ROW_ARGMAX) {
@@ -359,17 +360,49 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             // so each thread keeps its lowest column among equal keys.
             const uint32_t flip = op == ROW_MIN ? 0xffffffffu : 0u;
             uint32_t bk = 0, bc = 0;
+            // This thread's extreme with NaN-propagating three-input min/max
+            // (half an instruction per element).  Unless it is NaN or a zero,
+            // numeric order and key order agree on this thread's elements (only
+            // NaNs and the two zeros differ), so its key is the thread's best
+            // key, and argmax needs just the first column equal to it.
+            // Threads holding a NaN or a zero extreme run the full key scan.
+            const bool is_min = op == ROW_MIN;
+            float m = is_min ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 if (!valid(j)) continue;
-                const uint32_t col = (uint32_t)((tid + (uint64_t)j * BLOCK) * 4);
-                const float xs[4] = {c[j].x, c[j].y, c[j].z, c[j].w};
+                if (is_min)
+                    m = min3_nan(min3_nan(m, c[j].x, c[j].y), c[j].z, c[j].w);
+                else
+                    m = max3_nan(max3_nan(m, c[j].x, c[j].y), c[j].z, c[j].w);
+            }
+            if (m != m || m == 0.0f) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint32_t k = order_key(xs[e]) ^ flip;
-                    if (k > bk || (j == 0 && e == 0)) {
-                        bk = k;
-                        bc = col + e;
+                for (int j = 0; j < NV; ++j) {
+                    if (!valid(j)) continue;
+                    const uint32_t col = (uint32_t)((tid + (uint64_t)j * TB) * 4);
+                    const float xs[4] = {c[j].x, c[j].y, c[j].z, c[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t k = order_key(xs[e]) ^ flip;
+                        if (k > bk || (j == 0 && e == 0)) {
+                            bk = k;
+                            bc = col + e;
+                        }
+                    }
+                }
+            } else {
+                bk = order_key(m) ^ flip;
+                if (op == ROW_ARGMAX) {
+                    // last match wins in a reverse scan = first column
+#pragma unroll
+                    for (int j = NV - 1; j >= 0; --j) {
+                        if (!valid(j)) continue;
+                        const uint32_t col = (uint32_t)((tid + (uint64_t)j * TB) * 4);
+                        if (c[j].w == m) bc = col + 3;
+                        if (c[j].z == m) bc = col + 2;
+                        if (c[j].y == m) bc = col + 1;
+                        if (c[j].x == m) bc = col;
                     }
                 }
             }
@@ -385,7 +418,7 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             if (tid == 0) {
                 uint64_t t = s_k[par][0];
 #pragma unroll
-                for (int w = 1; w < BLOCK / 32; ++w) t = s_k[par][w] > t ? s_k[par][w] : t;
+                for (int w = 1; w < TB / 32; ++w) t = s_k[par][w] > t ? s_k[par][w] : t;
                 const uint32_t k = (uint32_t)(t >> 32) ^ flip;
                 if (op == ROW_ARGMAX)
                     static_cast<uint32_t*>(oa.data)[out_index(oa, row)] = 0xffffffffu - (uint32_t)(t & 0xffffffffu);
@@ -407,7 +440,7 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             }
             m = s_f[par][0];
 #pragma unroll
-            for (int w = 1; w < BLOCK / 32; ++w) m = fmaxf(m, s_f[par][w]);
+            for (int w = 1; w < TB / 32; ++w) m = fmaxf(m, s_f[par][w]);
             // exp(x - max) once per element (kept in registers for softmax);
             // each thread's terms are summed in f32, threads combine in f64.
             float e = 0.0f;
@@ -425,14 +458,14 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
             __syncthreads();
             ed = 0.0;
 #pragma unroll
-            for (int w = 0; w < BLOCK / 32; ++w) ed += s_d[1][par][w];
+            for (int w = 0; w < TB / 32; ++w) ed += s_d[1][par][w];
             if (op == STREAM_STATS + STATS_SOFTMAX) {
                 const float inv = (float)(1.0 / ed);
                 float* orow = eo.data + eo.offset + row * eo.row_stride;
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
                             make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv);
             } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
                 const double ls = log(ed);
@@ -441,52 +474,114 @@ __global__ void __launch_bounds__(BLOCK) rows_stream_kernel(Rows in, uint32_t op
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
                             make_float4(lsm(c[j].x), lsm(c[j].y), lsm(c[j].z), lsm(c[j].w));
             } else if (tid == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(ed));
             }
         } else {
-            // Moments / layer norm: f64 mean, then f64 centred squares, so any
-            // finite f32 input (up to f32::MAX) keeps a finite normalisation.
-            double a = 0.0;
+            // Moments / layer norm.  Both passes run in f32 with f64 accumulation
+            // of per-float4 partials, under error bounds that send a row back
+            // through f64 when they could approach the 1e-5 parity tolerance:
+            //  pass 1: s4 = pairwise f32 sum of 4 elements errs by at most
+            //          2u * sum|x| (u = 2^-24), so the mean is exact to
+            //          2u * A / n with A = sum|x| (f32 partials, f64 across);
+            //          accepted when that is <= 2^-20 * max(|mean|, 1),
+            //  pass 2: squares of d = x - m32 around the f32-rounded mean m32
+            //          (all terms >= 0: relative error a few u), corrected by
+            //          sum (x - m32)^2 = sum (x - mean)^2 + n * delta^2 with
+            //          delta = mean - m32; overflow (|d| > 1.8e19) or a sum
+            //          that might have underflowed falls back to f64.
+            // The reference computes both passes in f64 (statistics.cu:4-123).
+            double sd = 0.0;
+            float af = 0.0f;
 #pragma unroll
-            for (int j = 0; j < NV; ++j)
-                if (valid(j)) a += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
-            a = warp_sum(a);
-            if (lane == 0) s_d[0][par][warp] = a;
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) continue;
+                sd += (double)((c[j].x + c[j].y) + (c[j].z + c[j].w));
+                af += (fabsf(c[j].x) + fabsf(c[j].y)) + (fabsf(c[j].z) + fabsf(c[j].w));
+            }
+            sd = warp_sum(sd);
+            const double ad = warp_sum((double)af);
+            if (lane == 0) {
+                s_d[0][par][warp] = sd;
+                s_a[par][warp] = ad;
+            }
             barrier_release();
             if (s_abort) {
                 aborted_at = i;
                 break;
             }
-            a = 0.0;
+            double S = 0.0, A = 0.0;
 #pragma unroll
-            for (int w = 0; w < BLOCK / 32; ++w) a += s_d[0][par][w];
-            const double mean = a / (double)n;
-            double q = 0.0;
+            for (int w = 0; w < TB / 32; ++w) {
+                S += s_d[0][par][w];
+                A += s_a[par][w];
+            }
+            double mean = S / (double)n;
+            const double u = 5.9604644775390625e-08;  // 2^-24
+            if (!(fabs(mean) <= 1.7976931348623157e308) || !(2.0 * u * A / (double)n <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0))) {
+                // block-uniform fallback: exact f64 sum
+                double e = 0.0;
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j)) e += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
+                e = warp_sum(e);
+                __syncthreads();  // every thread has read the pass-1 partials of this parity
+                if (lane == 0) s_d[0][par][warp] = e;
+                __syncthreads();
+                e = 0.0;
+#pragma unroll
+                for (int w = 0; w < TB / 32; ++w) e += s_d[0][par][w];
+                mean = e / (double)n;
+            }
+            const float m32 = (float)mean;
+            const double delta = mean - (double)m32;
+            double qd = 0.0;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 if (!valid(j)) continue;
-                const double d0 = (double)c[j].x - mean, d1 = (double)c[j].y - mean;
-                const double d2 = (double)c[j].z - mean, d3 = (double)c[j].w - mean;
-                q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+                const float d0 = c[j].x - m32, d1 = c[j].y - m32, d2 = c[j].z - m32, d3 = c[j].w - m32;
+                qd += (double)(fmaf(d0, d0, d1 * d1) + fmaf(d2, d2, d3 * d3));
             }
-            q = warp_sum(q);
-            if (lane == 0) s_d[1][par][warp] = q;
+            qd = warp_sum(qd);
+            if (lane == 0) s_d[1][par][warp] = qd;
             __syncthreads();
-            q = 0.0;
+            double Q = 0.0;
 #pragma unroll
-            for (int w = 0; w < BLOCK / 32; ++w) q += s_d[1][par][w];
-            const double var = q / (double)n;
+            for (int w = 0; w < TB / 32; ++w) Q += s_d[1][par][w];
+            double var = Q / (double)n - delta * delta;
+            if (!(Q <= 1.7976931348623157e308) || Q < 1e-30 * (double)n) {
+                // block-uniform fallback: f64 centred squares (overflowing or
+                // vanishing f32 squares)
+                double e = 0.0;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    if (!valid(j)) continue;
+                    const double e0 = (double)c[j].x - mean, e1 = (double)c[j].y - mean;
+                    const double e2 = (double)c[j].z - mean, e3 = (double)c[j].w - mean;
+                    e += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+                }
+                e = warp_sum(e);
+                __syncthreads();
+                if (lane == 0) s_d[1][par][warp] = e;
+                __syncthreads();
+                e = 0.0;
+#pragma unroll
+                for (int w = 0; w < TB / 32; ++w) e += s_d[1][par][w];
+                var = e / (double)n;
+            }
+            if (var < 0.0) var = 0.0;
             if (op == STREAM_STATS + STATS_LAYER_NORM) {
                 const double inv = 1.0 / sqrt(var + (double)eps);
                 float* orow = eo.data + eo.offset + row * eo.row_stride;
-                auto ln = [&](float x) { return (float)(((double)x - mean) * inv); };
+                // (x - mean) * inv = (x - m32) * inv - delta * inv: one FFMA
+                const float invf = (float)inv, dinv = (float)(delta * inv);
+                auto ln = [&](float x) { return fmaf(x - m32, invf, -dinv); };
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * BLOCK) * 4) =
+                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
                             make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w));
             } else if (tid == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
@@ -652,26 +747,43 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
                          (in.rows <= 1 || eo.row_stride % 4 == 0)))
         return FB_ERR_UNSUPPORTED;
     const uint64_t vec = in.cols / 4;
-    const int nv = vec <= BLOCK ? 1 : vec <= 2 * BLOCK ? 2 : vec <= 4 * BLOCK ? 4 : 8;
+    // Operations with two block reductions per row (moments, layer norm,
+    // the softmax family) run 128-thread blocks with a two-row ring: twice as
+    // many rows in reduction at once per SM, which hides the per-row
+    // reduce/barrier latency; single-reduction ops keep 256 threads and a
+    // deeper ring.
+    const bool two_pass = op >= STREAM_STATS;
+    const uint32_t tb = two_pass && vec > 128 && vec <= 8 * 128 ? 128 : 256;
+    const int nv = vec <= tb ? 1 : vec <= 2 * tb ? 2 : vec <= 4 * tb ? 4 : 8;
+    if ((uint64_t)nv * 4 * tb < in.cols) return FB_ERR_UNSUPPORTED;
     // Ring depth: enough rows in flight to cover HBM latency, within shared memory.
     uint32_t stages = row_bytes <= 4096 ? 8 : row_bytes <= 8192 ? 5 : 3;
-    auto launch = [&](auto kernel) -> int {
+    if (tb == 128) stages = row_bytes <= 4096 ? 4 : 2;
+    auto launch = [&](auto kernel, uint32_t threads) -> int {
         const size_t smem = 128 + (size_t)stages * row_bytes;
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return FB_ERR_DRIVER;
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, BLOCK, smem) != cudaSuccess || per_sm < 1)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
             return FB_ERR_UNSUPPORTED;
         const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
         const unsigned grid = (unsigned)(in.rows < cap ? in.rows : cap);
-        kernel<<<grid, BLOCK, smem, st>>>(in, op, a, b, eo, eps, stages, (uint32_t)row_bytes);
+        kernel<<<grid, threads, smem, st>>>(in, op, a, b, eo, eps, stages, (uint32_t)row_bytes);
         return check_launch();
     };
+    if (tb == 128) {
+        switch (nv) {
+            case 1: return launch(rows_stream_kernel<T, 1, 128>, 128);
+            case 2: return launch(rows_stream_kernel<T, 2, 128>, 128);
+            case 4: return launch(rows_stream_kernel<T, 4, 128>, 128);
+            default: return launch(rows_stream_kernel<T, 8, 128>, 128);
+        }
+    }
     switch (nv) {
-        case 1: return launch(rows_stream_kernel<T, 1>);
-        case 2: return launch(rows_stream_kernel<T, 2>);
-        case 4: return launch(rows_stream_kernel<T, 4>);
-        default: return launch(rows_stream_kernel<T, 8>);
+        case 1: return launch(rows_stream_kernel<T, 1, 256>, 256);
+        case 2: return launch(rows_stream_kernel<T, 2, 256>, 256);
+        case 4: return launch(rows_stream_kernel<T, 4, 256>, 256);
+        default: return launch(rows_stream_kernel<T, 8, 256>, 256);
     }
 }
 
