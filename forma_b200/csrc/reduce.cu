@@ -284,8 +284,11 @@ __device__ __forceinline__ float4 smem_load4(const unsigned char* row, uint64_t 
 // Operation codes of the streamed engine: RowOp values, then StatsOp + 16.
 constexpr uint32_t STREAM_STATS = 16;
 
-template <typename T, int NV, int TB>
-__global__ void __launch_bounds__(TB) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
+// CAP: registers capped so that six 128-thread blocks fit per SM (argmax and
+// moments hold more per-row state and measured faster with the extra blocks;
+// the light reductions measured faster uncapped).
+template <typename T, int NV, int TB, bool CAP>
+__global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
                                                             float eps, uint32_t stages, uint32_t row_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -480,31 +483,54 @@ __global__ void __launch_bounds__(TB) rows_stream_kernel(Rows in, uint32_t op, R
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(ed));
             }
         } else {
-            // Moments / layer norm.  Both passes run in f32 with f64 accumulation
-            // of per-float4 partials, under error bounds that send a row back
-            // through f64 when they could approach the 1e-5 parity tolerance:
-            //  pass 1: s4 = pairwise f32 sum of 4 elements errs by at most
-            //          2u * sum|x| (u = 2^-24), so the mean is exact to
-            //          2u * A / n with A = sum|x| (f32 partials, f64 across);
-            //          accepted when that is <= 2^-20 * max(|mean|, 1),
-            //  pass 2: squares of d = x - m32 around the f32-rounded mean m32
-            //          (all terms >= 0: relative error a few u), corrected by
-            //          sum (x - m32)^2 = sum (x - mean)^2 + n * delta^2 with
-            //          delta = mean - m32; overflow (|d| > 1.8e19) or a sum
-            //          that might have underflowed falls back to f64.
-            // The reference computes both passes in f64 (statistics.cu:4-123).
-            double sd = 0.0;
-            float af = 0.0f;
+            // Moments / layer norm in one pass and one block reduction.  Each
+            // thread sums, per float4, x (pairwise f32, f64 across float4s),
+            // |x| (the error bound of that sum) and (x - a)^2 around an anchor
+            // a = the mean of the row's first four values (read from the staged
+            // row, identical in every thread).  Then
+            //   mean = S / n,   var = (Q - (S - n a)^2 / n) / n.
+            // Accepted when both error bounds leave a wide margin under the
+            // 1e-5 tolerance (u = 2^-24):
+            //   mean:  L u * A / n <= 2^-20 * max(|mean|, 1)   (A = sum |x|,
+            //          L = 2 + log2(NV): the depth of the f32 pairwise tree)
+            //   var:   Q <= 4 * n * var  (cancellation factor <= 4; each f32
+            //          partial of squares is within (L + 3) u, so var is
+            //          within 4 (L + 3) u, <= 28u)
+            // and everything is finite with a variance that cannot have
+            // underflowed in f32; otherwise (NaN/inf inputs, huge offsets
+            // from the anchor, constant rows) the row is redone exactly in f64
+            // with two passes, as the reference computes it (statistics.cu:4-123).
+            const float4 head = smem_load4<T>(rb, 0);
+            const float anc = 0.25f * ((head.x + head.y) + (head.z + head.w));
+            // per-float4 f32 partials, combined pairwise in f32 (depth log2(4 NV))
+            float s4[NV], q4[NV], a4[NV];
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
-                if (!valid(j)) continue;
-                sd += (double)((c[j].x + c[j].y) + (c[j].z + c[j].w));
-                af += (fabsf(c[j].x) + fabsf(c[j].y)) + (fabsf(c[j].z) + fabsf(c[j].w));
+                if (!valid(j)) {
+                    s4[j] = q4[j] = a4[j] = 0.0f;
+                    continue;
+                }
+                const float d0 = c[j].x - anc, d1 = c[j].y - anc, d2 = c[j].z - anc, d3 = c[j].w - anc;
+                s4[j] = (c[j].x + c[j].y) + (c[j].z + c[j].w);
+                q4[j] = fmaf(d0, d0, d1 * d1) + fmaf(d2, d2, d3 * d3);
+                a4[j] = (fabsf(c[j].x) + fabsf(c[j].y)) + (fabsf(c[j].z) + fabsf(c[j].w));
             }
+#pragma unroll
+            for (int w = 1; w < NV; w *= 2)
+#pragma unroll
+                for (int j = 0; j + w < NV; j += 2 * w) {
+                    s4[j] += s4[j + w];
+                    q4[j] += q4[j + w];
+                    a4[j] += a4[j + w];
+                }
+            double sd = (double)s4[0], qd = (double)q4[0];
+            const float af = a4[0];
             sd = warp_sum(sd);
+            qd = warp_sum(qd);
             const double ad = warp_sum((double)af);
             if (lane == 0) {
                 s_d[0][par][warp] = sd;
+                s_d[1][par][warp] = qd;
                 s_a[par][warp] = ad;
             }
             barrier_release();
@@ -512,65 +538,55 @@ __global__ void __launch_bounds__(TB) rows_stream_kernel(Rows in, uint32_t op, R
                 aborted_at = i;
                 break;
             }
-            double S = 0.0, A = 0.0;
+            double S = 0.0, Q = 0.0, A = 0.0;
 #pragma unroll
             for (int w = 0; w < TB / 32; ++w) {
                 S += s_d[0][par][w];
+                Q += s_d[1][par][w];
                 A += s_a[par][w];
             }
-            double mean = S / (double)n;
+            const double dn = (double)n;
+            double mean = S / dn;
+            const double Sd = S - dn * (double)anc;
+            double var = (Q - Sd * Sd / dn) / dn;
             const double u = 5.9604644775390625e-08;  // 2^-24
-            if (!(fabs(mean) <= 1.7976931348623157e308) || !(2.0 * u * A / (double)n <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0))) {
-                // block-uniform fallback: exact f64 sum
+            const double big = 1.7976931348623157e308;
+            const bool fast = fabs(S) <= big && Q <= big && A <= big && var > 1e-30 &&
+                              (2.0 + log2((double)NV)) * u * A / dn <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0) &&
+                              Q <= 4.0 * dn * var;
+            if (!fast) {
+                // block-uniform fallback: exact f64 two-pass (the partials of
+                // this parity are reused once every thread has read them)
                 double e = 0.0;
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j)) e += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
                 e = warp_sum(e);
-                __syncthreads();  // every thread has read the pass-1 partials of this parity
+                __syncthreads();
                 if (lane == 0) s_d[0][par][warp] = e;
                 __syncthreads();
                 e = 0.0;
 #pragma unroll
                 for (int w = 0; w < TB / 32; ++w) e += s_d[0][par][w];
-                mean = e / (double)n;
-            }
-            const float m32 = (float)mean;
-            const double delta = mean - (double)m32;
-            double qd = 0.0;
-#pragma unroll
-            for (int j = 0; j < NV; ++j) {
-                if (!valid(j)) continue;
-                const float d0 = c[j].x - m32, d1 = c[j].y - m32, d2 = c[j].z - m32, d3 = c[j].w - m32;
-                qd += (double)(fmaf(d0, d0, d1 * d1) + fmaf(d2, d2, d3 * d3));
-            }
-            qd = warp_sum(qd);
-            if (lane == 0) s_d[1][par][warp] = qd;
-            __syncthreads();
-            double Q = 0.0;
-#pragma unroll
-            for (int w = 0; w < TB / 32; ++w) Q += s_d[1][par][w];
-            double var = Q / (double)n - delta * delta;
-            if (!(Q <= 1.7976931348623157e308) || Q < 1e-30 * (double)n) {
-                // block-uniform fallback: f64 centred squares (overflowing or
-                // vanishing f32 squares)
-                double e = 0.0;
+                mean = e / dn;
+                double q = 0.0;
 #pragma unroll
                 for (int j = 0; j < NV; ++j) {
                     if (!valid(j)) continue;
                     const double e0 = (double)c[j].x - mean, e1 = (double)c[j].y - mean;
                     const double e2 = (double)c[j].z - mean, e3 = (double)c[j].w - mean;
-                    e += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+                    q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
                 }
-                e = warp_sum(e);
+                q = warp_sum(q);
+                if (lane == 0) s_d[1][par][warp] = q;
                 __syncthreads();
-                if (lane == 0) s_d[1][par][warp] = e;
-                __syncthreads();
-                e = 0.0;
+                q = 0.0;
 #pragma unroll
-                for (int w = 0; w < TB / 32; ++w) e += s_d[1][par][w];
-                var = e / (double)n;
+                for (int w = 0; w < TB / 32; ++w) q += s_d[1][par][w];
+                var = q / dn;
             }
+            const float m32 = (float)mean;
+            const double delta = mean - (double)m32;
             if (var < 0.0) var = 0.0;
             if (op == STREAM_STATS + STATS_LAYER_NORM) {
                 const double inv = 1.0 / sqrt(var + (double)eps);
@@ -747,13 +763,14 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
                          (in.rows <= 1 || eo.row_stride % 4 == 0)))
         return FB_ERR_UNSUPPORTED;
     const uint64_t vec = in.cols / 4;
-    // Operations with two block reductions per row (moments, layer norm,
-    // the softmax family) run 128-thread blocks with a two-row ring: twice as
-    // many rows in reduction at once per SM, which hides the per-row
-    // reduce/barrier latency; single-reduction ops keep 256 threads and a
-    // deeper ring.
-    const bool two_pass = op >= STREAM_STATS;
-    const uint32_t tb = two_pass && vec > 128 && vec <= 8 * 128 ? 128 : 256;
+    // Row reductions without an elementwise output (sum, min/max, argmax,
+    // mean, moments, logsumexp) run 128-thread blocks with a two-row ring:
+    // more rows in reduction at once per SM hides each row's reduce/barrier
+    // latency.  Operations that also write the row (softmax, log-softmax,
+    // layer norm) measured faster with 256 threads and a deeper ring.
+    const bool writes_row = op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
+                            op == STREAM_STATS + STATS_LAYER_NORM;
+    const uint32_t tb = !writes_row && vec > 128 && vec <= 8 * 128 ? 128 : 256;
     const int nv = vec <= tb ? 1 : vec <= 2 * tb ? 2 : vec <= 4 * tb ? 4 : 8;
     if ((uint64_t)nv * 4 * tb < in.cols) return FB_ERR_UNSUPPORTED;
     // Ring depth: enough rows in flight to cover HBM latency, within shared memory.
@@ -771,19 +788,28 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
         kernel<<<grid, threads, smem, st>>>(in, op, a, b, eo, eps, stages, (uint32_t)row_bytes);
         return check_launch();
     };
+    const bool cap = op == ROW_ARGMAX || op == STREAM_STATS + STATS_MOMENTS;
+    if (tb == 128 && cap) {
+        switch (nv) {
+            case 1: return launch(rows_stream_kernel<T, 1, 128, true>, 128);
+            case 2: return launch(rows_stream_kernel<T, 2, 128, true>, 128);
+            case 4: return launch(rows_stream_kernel<T, 4, 128, true>, 128);
+            default: return launch(rows_stream_kernel<T, 8, 128, true>, 128);
+        }
+    }
     if (tb == 128) {
         switch (nv) {
-            case 1: return launch(rows_stream_kernel<T, 1, 128>, 128);
-            case 2: return launch(rows_stream_kernel<T, 2, 128>, 128);
-            case 4: return launch(rows_stream_kernel<T, 4, 128>, 128);
-            default: return launch(rows_stream_kernel<T, 8, 128>, 128);
+            case 1: return launch(rows_stream_kernel<T, 1, 128, false>, 128);
+            case 2: return launch(rows_stream_kernel<T, 2, 128, false>, 128);
+            case 4: return launch(rows_stream_kernel<T, 4, 128, false>, 128);
+            default: return launch(rows_stream_kernel<T, 8, 128, false>, 128);
         }
     }
     switch (nv) {
-        case 1: return launch(rows_stream_kernel<T, 1, 256>, 256);
-        case 2: return launch(rows_stream_kernel<T, 2, 256>, 256);
-        case 4: return launch(rows_stream_kernel<T, 4, 256>, 256);
-        default: return launch(rows_stream_kernel<T, 8, 256>, 256);
+        case 1: return launch(rows_stream_kernel<T, 1, 256, false>, 256);
+        case 2: return launch(rows_stream_kernel<T, 2, 256, false>, 256);
+        case 4: return launch(rows_stream_kernel<T, 4, 256, false>, 256);
+        default: return launch(rows_stream_kernel<T, 8, 256, false>, 256);
     }
 }
 
