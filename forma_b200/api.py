@@ -202,7 +202,7 @@ def reduce_shape(op: int, shape: Sequence[int], axes: Sequence[int], keep_dims: 
 def _conv(fn, input, weight, options, out_dtype):
     dev = _device(input, weight)
     opts, _keep = _conv_options(options)
-    dims = conv_plan(list(input.shape), list(weight.shape), options) if True else None
+    dims = conv_plan(list(input.shape), list(weight.shape), options)
     out = torch.empty(dims, dtype=out_dtype, device=dev)
     di, dw, do = describe(input), describe(weight), describe(out)
     _check(fn(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
@@ -230,6 +230,15 @@ def conv_low_f32_into(input, weight, options, out):
     opts, _keep = _conv_options(options)
     di, dw, do = describe(input), describe(weight), describe(out)
     _check(lib().fb_conv_low_f32(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    return out
+
+
+def conv_low_into(input, weight, options, out):
+    """conv_low into a caller-provided 16-bit output view (e.g. channels-last)."""
+    dev = _device(input, weight)
+    opts, _keep = _conv_options(options)
+    di, dw, do = describe(input), describe(weight), describe(out)
+    _check(lib().fb_conv_low(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
     return out
 
 

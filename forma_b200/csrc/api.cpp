@@ -234,6 +234,43 @@ int row_stats_impl(uint32_t op, const fb_tensor* input, const uint32_t* axes_p, 
 
 // ------------------------------------------------------------ convolution
 
+// Launch arguments of a convolution: input/weight views, the output (or f32
+// result) view and the plan's geometry.
+ConvArgs conv_args(const View& in, const View& w, const View& res, const ConvPlan& plan) {
+    ConvArgs a;
+    a.input = in.data;
+    a.weight = w.data;
+    a.output = static_cast<float*>(res.data);
+    a.dtype = in.dtype;
+    a.spatial = plan.spatial_rank;
+    a.in_offset = in.offset;
+    a.w_offset = w.offset;
+    a.out_offset = res.offset;
+    a.batch = plan.output[0];
+    a.channels_per_group = plan.channels_per_group;
+    a.outputs_per_group = plan.outputs_per_group;
+    a.out_channels = plan.output[1];
+    a.in_stride_n = in.strides[0];
+    a.in_stride_c = in.strides[1];
+    a.w_stride_o = w.strides[0];
+    a.w_stride_c = w.strides[1];
+    a.out_stride_n = res.strides[0];
+    a.out_stride_c = res.strides[1];
+    a.out_count = res.count;
+    for (uint32_t d = 0; d < plan.spatial_rank; ++d) {
+        a.in_dims[d] = in.dims[d + 2];
+        a.out_dims[d] = plan.output[d + 2];
+        a.k_dims[d] = w.dims[d + 2];
+        a.in_strides[d] = in.strides[d + 2];
+        a.w_strides[d] = w.strides[d + 2];
+        a.out_strides[d] = res.strides[d + 2];
+        a.stride[d] = plan.strides[d];
+        a.dilation[d] = plan.dilations[d];
+        a.pad[d] = plan.pad_before[d];
+    }
+    return a;
+}
+
 int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
               void* stream, bool low, bool round_low) {
     View in, w, out;
@@ -263,6 +300,16 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
         for (uint64_t v : {plan.strides[d], plan.dilations[d], plan.pad_before[d], plan.pad_after[d]})
             if (v > 0xffffffffull) return fail(FB_ERR_INVALID_INPUT, "CUDA convolution coordinate exceeds u32");
 
+    // conv_low on the tensor-core path rounds in the GEMM epilogue and writes
+    // the 16-bit output directly; every other path computes an f32 result
+    // (in scratch for conv_low) and rounds it in a separate pass.
+    if (round_low && in.count > 0 && plan.channels_per_group > 0) {
+        ConvArgs d = conv_args(in, w, out, plan);
+        d.output = static_cast<float*>(out.data);
+        d.out_low = out.dtype;
+        const int st = launch_conv_tc(d, stream);
+        if (st != FB_ERR_UNSUPPORTED) return launched(st, "convolution");
+    }
     // f32 result buffer: the output itself, or scratch before low rounding.
     float* result = nullptr;
     View res = out;
@@ -285,37 +332,7 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
         int s = fill_view(res, 0u, stream);
         if (s != FB_OK) return s;
     } else {
-        ConvArgs a;
-        a.input = in.data;
-        a.weight = w.data;
-        a.output = static_cast<float*>(res.data);
-        a.dtype = in.dtype;
-        a.spatial = plan.spatial_rank;
-        a.in_offset = in.offset;
-        a.w_offset = w.offset;
-        a.out_offset = res.offset;
-        a.batch = plan.output[0];
-        a.channels_per_group = plan.channels_per_group;
-        a.outputs_per_group = plan.outputs_per_group;
-        a.out_channels = plan.output[1];
-        a.in_stride_n = in.strides[0];
-        a.in_stride_c = in.strides[1];
-        a.w_stride_o = w.strides[0];
-        a.w_stride_c = w.strides[1];
-        a.out_stride_n = res.strides[0];
-        a.out_stride_c = res.strides[1];
-        a.out_count = out.count;
-        for (uint32_t d = 0; d < plan.spatial_rank; ++d) {
-            a.in_dims[d] = in.dims[d + 2];
-            a.out_dims[d] = plan.output[d + 2];
-            a.k_dims[d] = w.dims[d + 2];
-            a.in_strides[d] = in.strides[d + 2];
-            a.w_strides[d] = w.strides[d + 2];
-            a.out_strides[d] = res.strides[d + 2];
-            a.stride[d] = plan.strides[d];
-            a.dilation[d] = plan.dilations[d];
-            a.pad[d] = plan.pad_before[d];
-        }
+        ConvArgs a = conv_args(in, w, res, plan);
         int s = FB_ERR_UNSUPPORTED;
         if (!low) s = launch_conv2d_f32_tiled(a, stream);
         if (low) s = launch_conv_tc(a, stream);

@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "async.cuh"
+#include "device_common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -43,8 +44,9 @@ struct ConvGemmParams {
     uint32_t k_blocks, c_blocks, S;
     int32_t pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
     uint32_t m_tiles, n_tiles;
-    uint32_t c_rows;  // 1: channels contiguous (s_c == 1) and 16-byte aligned rows
-    float* out;
+    uint32_t c_rows;  // 1: channels contiguous (s_c == 1) and aligned rows (16 B for f32, 8 B for 16-bit)
+    uint32_t out_low; // 0: f32 output; FB_BF16 / FB_F16: rounded once (nearest even) to that type
+    float* out;       // f32 output, or the 16-bit output's storage when out_low != 0
     uint64_t out_offset, s_n, s_c, s_p, s_q;
 };
 
@@ -210,13 +212,15 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
             tc_fence_after();
             const uint32_t mt = t / p.n_tiles, nt = t % p.n_tiles;
             const uint32_t m = mt * BM + row;
-            float* base = nullptr;
+            // element offset of this row's first column in the output (~0: no such row)
+            uint64_t base = ~0ull;
             if (m < p.M) {
                 const uint32_t pq = p.P * p.Q;
                 const uint32_t n = m / pq, r = m % pq;
-                base = p.out + p.out_offset + (uint64_t)n * p.s_n + (uint64_t)(r / p.Q) * p.s_p + (uint64_t)(r % p.Q) * p.s_q +
+                base = p.out_offset + (uint64_t)n * p.s_n + (uint64_t)(r / p.Q) * p.s_p + (uint64_t)(r % p.Q) * p.s_q +
                        (uint64_t)(nt * BN) * p.s_c;
             }
+            uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
             const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
             if (p.c_rows) {
                 // Channels contiguous: each row's 32-column chunk is 128
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                 // memory, then store it as float4 so that one instruction
                 // writes four whole 128-byte rows (8 lanes per row).
                 float* st = epi + quarter * (32 * C::EPI_PITCH);
-                const uint64_t my_base = base ? (uint64_t)(base - p.out) : ~0ull;
+                const uint64_t my_base = base;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     uint32_t v[32];
@@ -241,7 +245,14 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                         const int r = i * 4 + (lane >> 3), cc = lane & 7;
                         const uint64_t rb = __shfl_sync(0xffffffffu, my_base, r);
                         const float4 val = *reinterpret_cast<const float4*>(st + r * C::EPI_PITCH + 4 * cc);
-                        if (rb != ~0ull) *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
+                        if (rb != ~0ull) {
+                            if (p.out_low)
+                                *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
+                                    make_uint2(encode_low_pair(val.x, val.y, p.out_low),
+                                               encode_low_pair(val.z, val.w, p.out_low));
+                            else
+                                *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
+                        }
                     }
                     __syncwarp();
                 }
@@ -251,9 +262,19 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
-                    if (base) {
+                    if (base != ~0ull) {
+                        if (p.out_low == FB_BF16) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) base[(uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                            for (int j = 0; j < 32; ++j)
+                                out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_bf16(__uint_as_float(v[j]));
+                        } else if (p.out_low) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_f16(__uint_as_float(v[j]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                        }
                     }
                 }
             }
@@ -405,14 +426,16 @@ uint32_t read_gemm_status() {
     return v;
 }
 
-// Channels-contiguous output whose rows start on 16-byte boundaries: the
-// epilogue may store each row's 32-column chunks as float4.
+// Channels-contiguous output whose rows start on 16-byte (f32) or 8-byte
+// (16-bit) boundaries: the epilogue may store each row's 32-column chunks as
+// float4 / four packed 16-bit values.
 bool c_rows_ok(const ConvArgs& a) {
     if (a.out_stride_c != 1) return false;
     const uint64_t strides[3] = {a.out_stride_n, a.out_strides[0], a.out_strides[1]};
     for (uint64_t st : strides)
         if (st % 4 != 0) return false;
-    return (reinterpret_cast<uintptr_t>(a.output + a.out_offset) % 16) == 0;
+    const uint64_t esz = a.out_low ? 2 : 4;
+    return (reinterpret_cast<uintptr_t>(a.output) + a.out_offset * esz) % (4 * esz) == 0;
 }
 
 int launch_patches(const ConvArgs& a, void* stream) {
@@ -476,6 +499,7 @@ int launch_patches(const ConvArgs& a, void* stream) {
     p.s_p = a.out_strides[0];
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
+    p.out_low = a.out_low;
     switch (BN) {
         case 256: return launch_bn<256>(ta, tb, p, st);
         case 128: return launch_bn<128>(ta, tb, p, st);
@@ -578,6 +602,7 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.s_p = a.out_strides[0];
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
+    p.out_low = a.out_low;
     switch (BN) {
         case 256: return launch_bn<256>(ta, tb, p, st);
         case 128: return launch_bn<128>(ta, tb, p, st);

@@ -139,6 +139,10 @@ struct ConvArgs {
     uint64_t in_strides[3] = {0, 0, 0}, w_strides[3] = {0, 0, 0}, out_strides[3] = {0, 0, 0};
     uint64_t stride[3] = {1, 1, 1}, dilation[3] = {1, 1, 1}, pad[3] = {0, 0, 0};
     uint64_t out_count = 0;
+    // 0: `output` is f32.  FB_BF16 / FB_F16: `output` points at 16-bit storage
+    // and the result is rounded once (conv_low); only the tensor-core path
+    // accepts this, the others return FB_ERR_UNSUPPORTED for it.
+    uint32_t out_low = 0;
 };
 int launch_conv_direct(const ConvArgs& a, void* stream);
 // Returns FB_ERR_UNSUPPORTED when the geometry has no tiled kernel.

@@ -93,3 +93,32 @@ def test_tc_conv_c3_shapes_sampled(cuda):
             got = out[img:img + 1].cpu().numpy()
             err = float(np.abs(got - ref).max()) / float(np.abs(ref).max())
             assert err <= 1e-4, (c, img, err)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("channels_last_out", [False, True])
+def test_tc_conv_low_rounds_in_the_epilogue(cuda, dtype, channels_last_out):
+    """conv_low on the tensor-core path rounds the f32 accumulator once in the
+    GEMM epilogue: bit-identical to rounding conv_low_f32's result."""
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn(2, 14, 14, 256, generator=g).to(dtype).to(cuda).permute(0, 3, 1, 2)
+    w = (torch.randn(128, 3, 3, 256, generator=g) * 0.03).to(dtype).to(cuda).permute(0, 3, 1, 2)
+    o = ConvOptions([1, 1], [1, 1], [1, 1], [1, 1])
+    ref = api.cast_to_low(api.conv_low_f32(x, w, o), dtype)
+    if channels_last_out:
+        store = torch.empty(2, 14, 14, 128, dtype=dtype, device=cuda)
+        got = api.conv_low_into(x, w, o, store.permute(0, 3, 1, 2))
+    else:
+        got = api.conv_low(x, w, o)
+    assert api.device_status() == 0
+    assert torch.equal(got.contiguous().view(torch.int16).cpu(), ref.contiguous().view(torch.int16).cpu())
+
+
+def test_patch_conv_low_rounds_in_the_epilogue(cuda):
+    g = torch.Generator(device="cpu").manual_seed(12)
+    x = torch.randn(2, 3, 32, 32, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(128, 3, 16, 16, generator=g) * 0.03).bfloat16().to(cuda)
+    o = ConvOptions([16, 16], [1, 1], [0, 0], [0, 0])
+    ref = api.cast_to_low(api.conv_low_f32(x, w, o), torch.bfloat16)
+    got = api.conv_low(x, w, o)
+    assert torch.equal(got.view(torch.int16).cpu(), ref.view(torch.int16).cpu())
