@@ -244,15 +244,16 @@ def conv_low_into(input, weight, options, out):
 
 # ------------------------------------------------------------- attention
 
-def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions):
+def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions, out=None):
     dev = _device(query, key, value)
     kind = 0
     dm = None
     if mask is not None:
         kind = {"keep": 1, "additive": 2}[mask.kind]
-    dims = attention_plan(list(query.shape), list(key.shape), list(value.shape),
-                          list(mask.tensor.shape) if mask is not None else None, options)
-    out = torch.empty(dims, dtype=torch.float32, device=dev)
+    if out is None:
+        dims = attention_plan(list(query.shape), list(key.shape), list(value.shape),
+                              list(mask.tensor.shape) if mask is not None else None, options)
+        out = torch.empty(dims, dtype=torch.float32, device=dev)
     dq, dk, dv, do = describe(query), describe(key), describe(value), describe(out)
     if mask is not None:
         dm = describe(mask.tensor)
@@ -266,6 +267,11 @@ def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOp
 def attention(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):
     """softmax(scale * Q K^T + mask) V for f32 operands."""
     return _attention(lib().fb_attention, query, key, value, mask, options)
+
+
+def attention_low_f32_into(query, key, value, mask: Optional[Mask], options: AttentionOptions, out):
+    """attention_low_f32 into a caller-provided f32 output view (any row strides)."""
+    return _attention(lib().fb_attention_low_f32, query, key, value, mask, options, out)
 
 
 def attention_low_f32(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):

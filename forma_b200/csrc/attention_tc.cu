@@ -59,7 +59,9 @@ struct AttnParams {
     float scale_log2;       // scale * log2(e)
     float shift;            // log2 of the numerator pre-scale
     int32_t causal, causal_offset;
-    float* out;             // contiguous [..., L, D] f32
+    uint32_t k_batch_bcast, v_batch_bcast;  // K / V shared by every batch index (stride 0)
+    float* out;             // f32 rows: depth contiguous, rows at the strides below
+    uint64_t o_sb, o_sh, o_sl;              // output strides (elements) of batch, head, query
 };
 
 template <int D>
@@ -206,9 +208,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
 #pragma unroll
     for (int t = 0; t < QT; ++t) n_kv = max(n_kv, n_t[t]);
     const uint32_t batch = bh / p.H, head = bh % p.H;
-    const uint32_t kv_bh = batch * p.Hkv + head / (p.H / p.Hkv);
-    const int32_t q_row0 = (int32_t)(bh * p.L + q0);
-    const int32_t kv_row0 = (int32_t)(kv_bh * p.Lk);
+    const int32_t kv_head = (int32_t)(head / (p.H / p.Hkv));
+    // Tensor maps are 4-D {depth, rows, heads, batch}: rows past L / Lk read
+    // as zeros, and any row / head / batch strides are followed.
+    const int32_t k_b = p.k_batch_bcast ? 0 : (int32_t)batch, v_b = p.v_batch_bcast ? 0 : (int32_t)batch;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -239,7 +242,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             mbar_arrive_expect_tx(q_full, QT * C::Q_BYTES);
             for (int t = 0; t < QT; ++t)
                 for (int b = 0; b < C::BOXES; ++b)
-                    tma_load_2d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, q_row0 + t * TQ, q_full);
+                    tma_load_4d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, (int32_t)(q0 + t * TQ), (int32_t)head,
+                                (int32_t)batch, q_full);
         }
         uint32_t issued = 0;
         bool failed = false;
@@ -253,8 +257,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             unsigned char* vd = kd + C::K_BYTES;
             mbar_arrive_expect_tx(&kv_full[s], C::STAGE_BYTES);
             for (int b = 0; b < C::BOXES; ++b) {
-                tma_load_2d(kd + b * (TK * 128), &tmK, b * 64, kv_row0 + (int32_t)(j * TK), &kv_full[s]);
-                tma_load_2d(vd + b * (TK * 128), &tmV, b * 64, kv_row0 + (int32_t)(j * TK), &kv_full[s]);
+                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)(j * TK), kv_head, k_b, &kv_full[s]);
+                tma_load_4d(vd + b * (TK * 128), &tmV, b * 64, (int32_t)(j * TK), kv_head, v_b, &kv_full[s]);
             }
             ++issued;
         }
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         // `ok` and n are warp-uniform, so the loads are too; only the stores
         // depend on whether this row exists (q < L).
         const bool load = ok && n > 0;
-        float* orow = p.out + ((uint64_t)bh * p.L + q) * D;
+        float* orow = p.out + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + (uint64_t)q * p.o_sl;
         const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -481,49 +485,85 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_attn() {
     return fn;
 }
 
-// [rows, D] 16-bit rows, box {64, 128}, 128B swizzle.
-bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t rows, uint64_t D) {
+// One operand's rows as a 4-D box source {depth, rows, heads, batch}: element
+// strides of the row, head and (merged) batch axes; unit axes may have any
+// stride and a stride-0 batch axis (broadcast) becomes a single batch index.
+struct RowsLayout {
+    uint64_t rows = 0, heads = 1, batch = 1;
+    uint64_t s_row = 0, s_head = 0, s_batch = 0;
+    bool batch_bcast = false;
+};
+
+// Merges the batch axes [0, nb) of the row nest into one (count, stride):
+// the non-unit axes must nest row-major (stride[i] = stride[i+1] * dim[i+1])
+// or all have stride 0 (broadcast).
+bool merge_batch(const AttnArgs& a, const uint64_t* st, int nb, RowsLayout* o) {
+    uint64_t count = 1, stride = 0;
+    bool any = false, all_zero = true;
+    int last = -1;
+    for (int i = nb - 1; i >= 0; --i) {
+        if (a.row_dims[i] == 1) continue;
+        count *= a.row_dims[i];
+        if (st[i] != 0) all_zero = false;
+        if (!any) {
+            stride = st[i];
+            any = true;
+        } else if (st[i] != st[last] * a.row_dims[last]) {
+            if (!(st[i] == 0 && st[last] == 0)) return false;
+        }
+        last = i;
+    }
+    if (any && all_zero) {
+        o->batch = 1;
+        o->s_batch = 0;
+        o->batch_bcast = true;
+        return true;
+    }
+    if (any && stride == 0) return false;  // mixed broadcast and strided batch axes
+    o->batch = count;
+    o->s_batch = stride;
+    return true;
+}
+
+// [batch, heads, rows, D] 16-bit operand, box {64, box_rows, 1, 1}, 128B swizzle.
+bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t D, const RowsLayout& l, uint32_t box_rows) {
     auto enc = encode_tiled_attn();
     if (!enc) return false;
-    cuuint64_t dims[2] = {D, rows};
-    cuuint64_t strides[1] = {D * 2};
-    cuuint32_t box[2] = {64, 128};
-    cuuint32_t estr[2] = {1, 1};
-    return enc(map, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+    cuuint64_t dims[4] = {D, l.rows, l.heads, l.batch};
+    // byte strides of dims 1..3; unit dims get any valid stride (16-byte multiple)
+    uint64_t sb[3] = {l.s_row * 2, l.s_head * 2, l.s_batch * 2};
+    uint64_t filler = (D * 2 + 15) / 16 * 16;
+    for (int i = 0; i < 3; ++i) {
+        if (dims[i + 1] == 1 && (sb[i] == 0 || sb[i] % 16 != 0 || sb[i] >= (1ull << 40))) sb[i] = filler;
+        if (sb[i] == 0 || sb[i] % 16 != 0 || sb[i] >= (1ull << 40)) return false;
+        filler = sb[i] * dims[i + 1];
+        filler = (filler + 15) / 16 * 16;
+        if (filler >= (1ull << 40)) filler = 16;
+    }
+    cuuint64_t strides[3] = {sb[0], sb[1], sb[2]};
+    cuuint32_t box[4] = {64, box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int i = 0; i < 4; ++i)
+        if (dims[i] == 0 || dims[i] > (1ull << 31)) return false;
+    return enc(map, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr),
                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Rows of a [..., heads, L, D] operand are dense when every row-nest stride
-// equals D times the product of the inner row dims (heads use `heads`).
-bool dense_rows(const AttnArgs& a, const uint64_t* strides, uint64_t heads, uint64_t L, uint64_t D, bool kv) {
-    const int r = (int)a.row_rank;
-    // queries axis
-    if (!kv && strides[r - 1] != D) return false;
-    uint64_t expect = L * D;
-    if (strides[r - 2] != expect && heads > 1) return false;
-    expect *= heads;
-    for (int i = r - 3; i >= 0; --i) {
-        if (a.row_dims[i] > 1 && strides[i] != expect) return false;
-        expect *= a.row_dims[i];
-    }
-    return true;
-}
-
 template <int D>
-int launch_d(const AttnArgs& a, uint32_t fmt, cudaStream_t st) {
+int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLayout& kl, const RowsLayout& vl,
+             const RowsLayout& ol, cudaStream_t st) {
     using C = ACfg<D>;
     const int r = (int)a.row_rank;
     const uint64_t L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
     const uint64_t BH = a.rows / L;
-    const uint64_t B = BH / H;
     const uint64_t Hkv = H / a.group_size;
     CUtensorMap tq, tk, tv;
     const void* q = static_cast<const uint16_t*>(a.q) + a.q_offset;
     const void* k = static_cast<const uint16_t*>(a.k) + a.k_offset;
     const void* v = static_cast<const uint16_t*>(a.v) + a.v_offset;
-    if (!make_rows_map(&tq, q, fmt, BH * L, D) || !make_rows_map(&tk, k, fmt, B * Hkv * Lk, D) ||
-        !make_rows_map(&tv, v, fmt, B * Hkv * Lk, D))
+    if (!make_rows_map(&tq, q, fmt, D, ql, TQ) || !make_rows_map(&tk, k, fmt, D, kl, TK) ||
+        !make_rows_map(&tv, v, fmt, D, vl, TK))
         return FB_ERR_UNSUPPORTED;
     AttnParams p{};
     p.fmt = fmt;
@@ -542,7 +582,12 @@ int launch_d(const AttnArgs& a, uint32_t fmt, cudaStream_t st) {
     p.shift = fmt ? 9.0f + std::ceil(std::log2((float)std::max<uint64_t>(Lk, 1))) : 0.0f;
     p.causal = a.causal ? 1 : 0;
     p.causal_offset = a.causal_offset;
+    p.k_batch_bcast = kl.batch_bcast ? 1 : 0;
+    p.v_batch_bcast = vl.batch_bcast ? 1 : 0;
     p.out = a.out + a.o_offset;
+    p.o_sb = ol.s_batch;
+    p.o_sh = ol.s_head;
+    p.o_sl = ol.s_row;
     auto kernel = attn_fwd_kernel<D>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return launch_status("shared-memory attribute");
@@ -571,24 +616,34 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
     const int r = (int)a.row_rank;
     const uint64_t D = a.depth, L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
     if (a.q_stride_d != 1 || a.k_stride_d != 1 || a.v_stride_d != 1 || a.o_stride_d != 1) return FB_ERR_UNSUPPORTED;
-    if (a.k_stride_key != D || a.v_stride_key != D) return FB_ERR_UNSUPPORTED;
     if (H % a.group_size != 0) return FB_ERR_UNSUPPORTED;
     const uint64_t Hkv = H / a.group_size;
-    if (!dense_rows(a, a.q_row_strides, H, L, D, false) || !dense_rows(a, a.o_row_strides, H, L, D, false) ||
-        !dense_rows(a, a.k_row_strides, Hkv, Lk, D, true) || !dense_rows(a, a.v_row_strides, Hkv, Lk, D, true))
+    if (a.rows / L * L != a.rows || L > (1u << 30) || Lk > (1u << 30)) return FB_ERR_UNSUPPORTED;
+    // Row layouts: query/key axis, head axis (K/V heads are query heads /
+    // group), batch axes merged; TMA needs 16-byte strides and bases.
+    RowsLayout ql, kl, vl, ol;
+    ql.rows = L, ql.heads = H, ql.s_row = a.q_row_strides[r - 1], ql.s_head = a.q_row_strides[r - 2];
+    kl.rows = Lk, kl.heads = Hkv, kl.s_row = a.k_stride_key, kl.s_head = a.k_row_strides[r - 2];
+    vl.rows = Lk, vl.heads = Hkv, vl.s_row = a.v_stride_key, vl.s_head = a.v_row_strides[r - 2];
+    ol.rows = L, ol.heads = H, ol.s_row = a.o_row_strides[r - 1], ol.s_head = a.o_row_strides[r - 2];
+    if (!merge_batch(a, a.q_row_strides, r - 2, &ql) || !merge_batch(a, a.k_row_strides, r - 2, &kl) ||
+        !merge_batch(a, a.v_row_strides, r - 2, &vl) || !merge_batch(a, a.o_row_strides, r - 2, &ol))
         return FB_ERR_UNSUPPORTED;
-    // 16-byte aligned operand bases (TMA) and 16-byte aligned output rows.
+    if (ql.batch_bcast || ol.batch_bcast) return FB_ERR_UNSUPPORTED;  // distinct query rows per batch index
+    if (ql.batch * H * L != a.rows || ol.batch != ql.batch) return FB_ERR_UNSUPPORTED;
+    if ((!kl.batch_bcast && kl.batch != ql.batch) || (!vl.batch_bcast && vl.batch != ql.batch)) return FB_ERR_UNSUPPORTED;
+    // f32 output rows take float4 stores: 16-byte aligned rows
+    auto mult4 = [](uint64_t s, uint64_t n) { return n <= 1 || s % 4 == 0; };
+    if (!mult4(ol.s_row, L) || !mult4(ol.s_head, H) || !mult4(ol.s_batch, ol.batch)) return FB_ERR_UNSUPPORTED;
     auto aligned = [](const void* p, uint64_t off, uint64_t esz) {
         return (reinterpret_cast<uintptr_t>(p) + off * esz) % 16 == 0;
     };
     if (!aligned(a.q, a.q_offset, 2) || !aligned(a.k, a.k_offset, 2) || !aligned(a.v, a.v_offset, 2) ||
         !aligned(a.out, a.o_offset, 4))
         return FB_ERR_UNSUPPORTED;
-    if (a.rows / L * L != a.rows || a.rows * D > (1ull << 40) || L > (1u << 30) || Lk > (1u << 30))
-        return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return D == 64 ? launch_d<64>(a, fmt, st) : launch_d<128>(a, fmt, st);
+    return D == 64 ? launch_d<64>(a, fmt, ql, kl, vl, ol, st) : launch_d<128>(a, fmt, ql, kl, vl, ol, st);
 }
 
 }  // namespace fb

@@ -171,6 +171,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            int32_t w, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // im2col load of a 4-D NHWC tensor: `pixels_per_column` consecutive output
 // pixels starting at base pixel (w, h, n), each shifted by the filter tap
 // (off_w, off_h), channels [c, c + channels_per_pixel).

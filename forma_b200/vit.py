@@ -8,7 +8,7 @@ joined by residual additions and a GELU.  Pre-norm blocks::
     x  = [cls; patches(img) W_p] + pos                 conv 16x16 stride 16
     for each layer:
         h  = LN(x)                                     layer_norm, eps 1e-5
-        q, k, v = heads(h W_qkv)                       1x1 conv, cast per head
+        q, k, v = heads(h W_qkv)                       1x1 conv rounded to BF16 in its epilogue
         x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv
         h  = LN(x)
         x  = x + GELU(h W_1) W_2                        1x1 convs
@@ -111,10 +111,8 @@ class ViTEncoder:
             "x": torch.empty(B, L, E, device=dev),
             "patches": torch.empty(B, G, G, E, device=dev),      # channels-last conv result
             "h_low": torch.empty(B, L, E, dtype=low, device=dev),
-            "qkv": torch.empty(B, 1, L, 3 * E, device=dev),
-            "q": torch.empty(B, H, L, D, dtype=low, device=dev),
-            "k": torch.empty(B, H, L, D, dtype=low, device=dev),
-            "v": torch.empty(B, H, L, D, dtype=low, device=dev),
+            "qkv_low": torch.empty(B, 1, L, 3 * E, dtype=low, device=dev),   # [B, L, 3, H, D] rounded once
+            "a": torch.empty(B, L, E, device=dev),                          # attention output, [B, L, H, D] order
             "a_low": torch.empty(B, L, E, dtype=low, device=dev),
             "o": torch.empty(B, 1, L, E, device=dev),
             "m": torch.empty(B, 1, L, M, device=dev),
@@ -146,12 +144,15 @@ class ViTEncoder:
             # attention sub-block
             h = api.layer_norm(x, [2], cfg.eps)
             api.cast_to_low_into(h, b["h_low"])
-            self._proj(b["h_low"], blk["qkv"], b["qkv"])
-            qkv = b["qkv"].view(B, L, 3, H, D)
-            for i, name in enumerate(("q", "k", "v")):
-                api.cast_to_low_into(qkv[:, :, i].permute(0, 2, 1, 3), b[name])
-            a = api.attention_low_f32(b["q"], b["k"], b["v"], None, opts)
-            api.cast_to_low_into(a.permute(0, 2, 1, 3), b["a_low"].view(B, L, H, D))
+            # QKV rounded once in the GEMM epilogue (conv_low), read by the
+            # attention kernel as head-interleaved views of one buffer
+            xin = b["h_low"].view(B, 1, L, E).permute(0, 3, 1, 2)
+            api.conv_low_into(xin, blk["qkv"], ConvOptions([1, 1], [1, 1], [0, 0], [0, 0]),
+                              b["qkv_low"].permute(0, 3, 1, 2))
+            qkv = b["qkv_low"].view(B, L, 3, H, D)
+            q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))   # [B, H, L, D] views
+            api.attention_low_f32_into(q, k, v, None, opts, b["a"].view(B, L, H, D).permute(0, 2, 1, 3))
+            api.cast_to_low_into(b["a"], b["a_low"])
             self._proj(b["a_low"], blk["proj"], b["o"])
             api.add(x, b["o"].view(B, L, E), out=x)
             # MLP sub-block

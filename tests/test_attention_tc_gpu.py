@@ -77,3 +77,46 @@ def test_tc_attention_c4_size_sampled(cuda):
         got = out[b, h].cpu().numpy()
         err = float(np.abs(got - ref).max()) / float(np.abs(ref).max())
         assert err <= 5e-3, (b, h, err)
+
+
+def _check_views(cuda, q, k, v, out=None, causal=None, tol=2e-2):
+    """q/k/v (and out) are strided device views; the oracle sees dense copies."""
+    before = api.launch_count()
+    if out is None:
+        got = api.attention_low_f32(q, k, v, None, AttentionOptions(None, causal))
+    else:
+        got = api.attention_low_f32_into(q, k, v, None, AttentionOptions(None, causal), out)
+    assert api.device_status() == 0
+    assert api.launch_count() > before
+    ref = orc.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), None, None,
+                        causal, nthreads=orc.threads())
+    g = got.cpu().numpy()
+    err = float(np.abs(g.astype(np.float64) - ref).max()) / max(float(np.abs(ref).max()), 1e-30)
+    assert err <= tol, err
+
+
+def test_tc_attention_blhd_views_and_strided_output(cuda):
+    # [B, L, H, D] storage viewed as [B, H, L, D], output written in [B, L, H, D] order
+    g = torch.Generator(device="cpu").manual_seed(21)
+    B, L, H, D = 2, 300, 4, 64
+    q, k, v = (torch.randn(B, L, H, D, generator=g).bfloat16().to(cuda).permute(0, 2, 1, 3) for _ in range(3))
+    store = torch.empty(B, L, H, D, device=cuda)
+    _check_views(cuda, q, k, v, store.permute(0, 2, 1, 3), causal=0)
+
+
+def test_tc_attention_interleaved_qkv_buffer(cuda):
+    # one [B, L, 3, H, D] buffer (a fused QKV projection's output); D = 128
+    g = torch.Generator(device="cpu").manual_seed(22)
+    B, L, H, D = 2, 256, 2, 128
+    qkv = torch.randn(B, L, 3, H, D, generator=g).bfloat16().to(cuda)
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    _check_views(cuda, q, k, v)
+
+
+def test_tc_attention_broadcast_kv_batch(cuda):
+    # K/V shared by every batch index (stride 0), GQA with 2 query heads per K/V head
+    g = torch.Generator(device="cpu").manual_seed(23)
+    q = torch.randn(3, 4, 192, 64, generator=g).bfloat16().to(cuda)
+    k = torch.randn(1, 2, 192, 64, generator=g).bfloat16().to(cuda).expand(3, 2, 192, 64)
+    v = torch.randn(1, 2, 192, 64, generator=g).bfloat16().to(cuda).expand(3, 2, 192, 64)
+    _check_views(cuda, q, k, v, causal=0)
