@@ -377,6 +377,36 @@ def layer_norm(input: torch.Tensor, axes: Sequence[int], epsilon: float) -> torc
     return _normalize(lib().fb_layer_norm, input, list(axes), float(epsilon))
 
 
+def _normalize_low(fn, input, axes, dtype, eps=None, out=None):
+    dev = _device(input)
+    if out is None:
+        out = torch.empty(list(input.shape), dtype=dtype, device=dev)
+    ax = _lib.u32_array(axes)
+    di, do = describe(input), describe(out)
+    if eps is None:
+        _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev)))
+    else:
+        _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev)))
+    return out
+
+
+def softmax_low(input: torch.Tensor, axes: Sequence[int]) -> torch.Tensor:
+    """softmax_low: f16/bf16 input, result rounded once to the input dtype."""
+    return _normalize_low(lib().fb_softmax, input, axes, input.dtype)
+
+
+def log_softmax_low(input: torch.Tensor, axes: Sequence[int]) -> torch.Tensor:
+    """log_softmax_low: f16/bf16 input, result rounded once to the input dtype."""
+    return _normalize_low(lib().fb_log_softmax, input, axes, input.dtype)
+
+
+def layer_norm_low(input: torch.Tensor, axes: Sequence[int], epsilon: float, dtype: Optional[torch.dtype] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """layer_norm_low: result rounded once to ``dtype`` (the input's 16-bit dtype
+    for the trait method; an f32 input may name bf16/f16 explicitly)."""
+    return _normalize_low(lib().fb_layer_norm, input, axes, dtype or input.dtype, epsilon, out)
+
+
 def logsumexp(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -> torch.Tensor:
     dev = _device(input)
     dims = reduce_shape(ReduceOp.Sum, list(input.shape), list(axes), keep_dims, True)

@@ -181,21 +181,50 @@ int normalize_impl(uint32_t op, const fb_tensor* input, const uint32_t* axes_p, 
     FB_TRY(validate_axes(in.dims, axes));  // normalization_shape
     if (op == STATS_LAYER_NORM && (!std::isfinite(eps) || eps <= 0.0f))
         return fail(FB_ERR_INVALID_EPSILON, "normalization epsilon must be finite and strictly positive");
-    FB_TRY(check_output(output, "output", in.dims, FB_F32, &out));
+    // An output of the input's 16-bit dtype is the reference's `_low` form
+    // (the f32 result cast once to low storage: low_statistics.rs:59-108).
+    // An f32 input may also take a 16-bit output (same single rounding; for
+    // programs that feed the result to a low-precision contraction).
+    const bool low_out = output && is_low(output->dtype) && (output->dtype == in.dtype || in.dtype == FB_F32);
+    FB_TRY(check_output(output, "output", in.dims, low_out ? output->dtype : FB_F32, &out));
+    if (low_out && !is_contiguous(out)) return fail(FB_ERR_INVALID_INPUT, "low statistics output must be contiguous");
     if (in.count == 0) return FB_OK;
     Dims reduced;
     FB_TRY(reduce_dims(in.dims, axes, false, &reduced));
     uint64_t rows;
     FB_TRY(numel(reduced, &rows));
+    Rows r = make_rows(in, axes);
+    RowOut none;
+    if (low_out && rows != in.count) {
+        // rounded in the streamed row engine's store when it takes the rows
+        ElemOut e = make_elem_out(out, axes);
+        e.dtype = out.dtype;
+        const int st = launch_stats_rows(op, r, e, none, none, eps, stream);
+        if (st != FB_ERR_UNSUPPORTED) return launched(st, "statistics");
+    }
+    // f32 result: the output itself, or scratch before the low rounding
+    View res = out;
+    if (low_out) {
+        float* buf = static_cast<float*>(scratch(stream, out.count * 4 + 256, SCRATCH_STATS));
+        if (!buf) return fail(FB_ERR_DRIVER, "scratch allocation failed");
+        res.data = buf;
+        res.offset = 0;
+        res.dtype = FB_F32;  // contiguous, like `out`
+    }
+    int st;
     if (rows == in.count) {
         // Singleton groups: softmax 1, log-softmax and layer norm 0
         // (compute-cuda/src/statistics.rs:104-126).
-        return fill_view(out, op == STATS_SOFTMAX ? f32_bits(1.0f) : 0u, stream);
+        st = fill_view(res, op == STATS_SOFTMAX ? f32_bits(1.0f) : 0u, stream);
+    } else {
+        ElemOut e = make_elem_out(res, axes);
+        st = launched(launch_stats_rows(op, r, e, none, none, eps, stream), "statistics");
     }
-    Rows r = make_rows(in, axes);
-    ElemOut e = make_elem_out(out, axes);
-    RowOut none;
-    return launched(launch_stats_rows(op, r, e, none, none, eps, stream), "statistics");
+    if (st != FB_OK || !low_out) return st;
+    Nest rn = make_nest(res.dims, res.strides, all_axes(res.dims.size()));
+    return launched(launch_cast_to_low(static_cast<float*>(res.data), 0, rn,
+                                       static_cast<uint16_t*>(out.data) + out.offset, out.dtype, out.count, stream),
+                    "cast");
 }
 
 int row_stats_impl(uint32_t op, const fb_tensor* input, const uint32_t* axes_p, uint32_t n_axes, int32_t keep,

@@ -43,11 +43,14 @@ struct RowOut {
 
 // Destination with the input's geometry (softmax, log-softmax, layer norm).
 struct ElemOut {
-    float* data = nullptr;
+    float* data = nullptr;  // storage base (16-bit storage when dtype is F16/BF16)
     uint64_t offset = 0;
     Nest outer, inner;
     bool contiguous_rows = false;
     uint64_t row_stride = 0;
+    // FB_F32, or FB_F16/FB_BF16: rounded once (nearest even) on store; only
+    // the streamed row engine writes 16-bit rows (others: FB_ERR_UNSUPPORTED)
+    uint32_t dtype = FB_F32;
 };
 
 enum RowOp : uint32_t {
@@ -76,7 +79,8 @@ enum ScratchSlot : int {
     SCRATCH_CONV_RESULT = 1,  // f32 convolution result before low rounding
     SCRATCH_CONV_WEIGHT = 2,  // weights gathered into [O, kh, kw, C] or [O, C, kh, kw]
     SCRATCH_CONV_PATCH = 3,   // non-overlapping patches gathered into [N*P*Q, C*kh*kw]
-    SCRATCH_SLOTS = 4,
+    SCRATCH_STATS = 4,        // f32 statistics result before low rounding
+    SCRATCH_SLOTS = 5,
 };
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();

@@ -43,6 +43,17 @@ __device__ __forceinline__ uint64_t out_index(const RowOut& o, uint64_t row) {
     return o.offset + (o.contiguous ? row : nest_offset(o.nest, row));
 }
 
+// Four consecutive results of a contiguous row, as f32 or rounded 16-bit.
+__device__ __forceinline__ void store_row4(const ElemOut& eo, uint64_t row, uint64_t col, float4 v) {
+    const uint64_t i = eo.offset + row * eo.row_stride + col;
+    if (eo.dtype == FB_F32) {
+        *reinterpret_cast<float4*>(eo.data + i) = v;
+    } else {
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(eo.data) + i) =
+            make_uint2(encode_low_pair(v.x, v.y, eo.dtype), encode_low_pair(v.z, v.w, eo.dtype));
+    }
+}
+
 __device__ __forceinline__ float* elem_out(const ElemOut& o, uint64_t row, uint64_t c) {
     if (o.contiguous_rows) return o.data + o.offset + row * o.row_stride + c;
     return o.data + o.offset + nest_offset(o.outer, row) + nest_offset(o.inner, c);
@@ -463,21 +474,19 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
             for (int w = 0; w < TB / 32; ++w) ed += s_d[1][par][w];
             if (op == STREAM_STATS + STATS_SOFTMAX) {
                 const float inv = (float)(1.0 / ed);
-                float* orow = eo.data + eo.offset + row * eo.row_stride;
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
-                            make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv);
+                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
+                                   make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv));
             } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
                 const double ls = log(ed);
-                float* orow = eo.data + eo.offset + row * eo.row_stride;
                 auto lsm = [&](float x) { return (float)(((double)x - (double)m) - ls); };
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
-                            make_float4(lsm(c[j].x), lsm(c[j].y), lsm(c[j].z), lsm(c[j].w));
+                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
+                                   make_float4(lsm(c[j].x), lsm(c[j].y), lsm(c[j].z), lsm(c[j].w)));
             } else if (tid == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(ed));
             }
@@ -587,15 +596,14 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
             if (var < 0.0) var = 0.0;
             if (op == STREAM_STATS + STATS_LAYER_NORM) {
                 const double inv = 1.0 / sqrt(var + (double)eps);
-                float* orow = eo.data + eo.offset + row * eo.row_stride;
                 // (x - mean) * inv = (x - m32) * inv - delta * inv: one FFMA
                 const float invf = (float)inv, dinv = (float)(delta * inv);
                 auto ln = [&](float x) { return fmaf(x - m32, invf, -dinv); };
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
-                        *reinterpret_cast<float4*>(orow + (tid + (uint64_t)j * TB) * 4) =
-                            make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w));
+                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
+                                   make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w)));
             } else if (tid == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
                 static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
@@ -756,7 +764,8 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
     if (addr % 16 != 0 || (in.rows > 1 && (in.row_stride * esz) % 16 != 0)) return FB_ERR_UNSUPPORTED;
     const bool elementwise = op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
                              op == STREAM_STATS + STATS_LAYER_NORM;
-    if (elementwise && !(eo.contiguous_rows && reinterpret_cast<uintptr_t>(eo.data + eo.offset) % 16 == 0 &&
+    const uint64_t oesz = eo.dtype == FB_F32 ? 4 : 2;
+    if (elementwise && !(eo.contiguous_rows && (reinterpret_cast<uintptr_t>(eo.data) + eo.offset * oesz) % (4 * oesz) == 0 &&
                          (in.rows <= 1 || eo.row_stride % 4 == 0)))
         return FB_ERR_UNSUPPORTED;
     const uint64_t vec = in.cols / 4;
@@ -855,6 +864,7 @@ int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const Row
     if (in.rows == 0) return FB_OK;
     const int r = stream_rows(STREAM_STATS + op, in, a, b, out, eps, s);
     if (r != FB_ERR_UNSUPPORTED) return r;
+    if (out.dtype != FB_F32) return FB_ERR_UNSUPPORTED;  // 16-bit rows: streamed engine only
     switch (in.dtype) {
         case FB_F32: return stats_typed<float>(op, in, out, a, b, eps, s);
         case FB_BF16: return stats_typed<__nv_bfloat16>(op, in, out, a, b, eps, s);

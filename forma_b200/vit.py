@@ -7,7 +7,7 @@ joined by residual additions and a GELU.  Pre-norm blocks::
 
     x  = [cls; patches(img) W_p] + pos                 conv 16x16 stride 16
     for each layer:
-        h  = LN(x)                                     layer_norm, eps 1e-5
+        h  = LN(x)                                     layer_norm, eps 1e-5, rounded to BF16 as stored
         q, k, v = heads(h W_qkv)                       1x1 conv rounded to BF16 in its epilogue
         x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv
         h  = LN(x)
@@ -142,8 +142,7 @@ class ViTEncoder:
         opts = AttentionOptions()  # default scale 1/sqrt(D), non-causal
         for blk in self.blocks:
             # attention sub-block
-            h = api.layer_norm(x, [2], cfg.eps)
-            api.cast_to_low_into(h, b["h_low"])
+            api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])  # rounded as stored
             # QKV rounded once in the GEMM epilogue (conv_low), read by the
             # attention kernel as head-interleaved views of one buffer
             xin = b["h_low"].view(B, 1, L, E).permute(0, 3, 1, 2)
@@ -156,8 +155,7 @@ class ViTEncoder:
             self._proj(b["a_low"], blk["proj"], b["o"])
             api.add(x, b["o"].view(B, L, E), out=x)
             # MLP sub-block
-            h = api.layer_norm(x, [2], cfg.eps)
-            api.cast_to_low_into(h, b["h_low"])
+            api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])
             self._proj(b["h_low"], blk["fc1"], b["m"])
             api.gelu_to_low(b["m"], self.dtype, out=b["m_low"])
             self._proj(b["m_low"].view(B, L, M), blk["fc2"], b["o"])

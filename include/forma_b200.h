@@ -266,7 +266,12 @@ uint64_t fb_sum_static_max_elements(void);
 /* TensorStatsBackend (tensor-core/src/statistics.rs:100-129; replaces
  * compute-cuda/src/statistics.rs:45-252).  Inputs are F32, or F16/BF16 for
  * the *_low_f32 trait methods (tensor-core/src/low_statistics.rs:25-57),
- * selected by the input dtype; outputs are always f32. */
+ * selected by the input dtype; outputs are f32.  fb_softmax, fb_log_softmax
+ * and fb_layer_norm also take a contiguous output of the input's F16/BF16
+ * dtype: the *_low trait methods (low_statistics.rs:59-108, the f32 result
+ * rounded once, nearest even), rounded as the rows are stored.  An F32 input
+ * with an F16/BF16 output is rounded the same way (no counterpart in the
+ * reference trait; for programs that feed a low-precision contraction). */
 int fb_softmax(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes,
                fb_tensor* output, void* stream);
 int fb_log_softmax(const fb_tensor* input, const uint32_t* axes,

@@ -287,3 +287,31 @@ def test_full_size_row_workload_properties(cuda):
     tot = api.global_sum(x).item()
     want = x.double().sum().item()
     assert abs(tot - want) <= 1e-5 * max(abs(want), 1.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape,axes", [((64, 4096), [1]), ((6, 768), [1]), ((33, 17), [0])])
+def test_low_statistics_round_once(cuda, dtype, shape, axes):
+    """softmax_low / log_softmax_low / layer_norm_low (low_statistics.rs:59-108):
+    the f32 result rounded once to the input dtype, whether the row engine
+    rounds while storing (contiguous rows) or the result goes through scratch
+    (other axes)."""
+    g = torch.Generator(device="cpu").manual_seed(31)
+    x = (torch.randn(*shape, generator=g) * 3).to(dtype).to(cuda)
+    pairs = [
+        (api.softmax_low(x, axes), api.softmax(x, axes)),
+        (api.log_softmax_low(x, axes), api.log_softmax(x, axes)),
+        (api.layer_norm_low(x, axes, 1e-5), api.layer_norm(x, axes, 1e-5)),
+    ]
+    for got, f32 in pairs:
+        assert got.dtype == dtype
+        ref = api.cast_to_low(f32, dtype)
+        assert torch.equal(got.view(torch.int16).cpu(), ref.view(torch.int16).cpu())
+
+
+def test_layer_norm_f32_input_low_output(cuda):
+    g = torch.Generator(device="cpu").manual_seed(32)
+    x = torch.randn(8, 197, 768, generator=g).to(cuda)
+    got = api.layer_norm_low(x, [2], 1e-5, torch.bfloat16)
+    ref = api.cast_to_low(api.layer_norm(x, [2], 1e-5), torch.bfloat16)
+    assert torch.equal(got.view(torch.int16).cpu(), ref.view(torch.int16).cpu())
