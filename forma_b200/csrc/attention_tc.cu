@@ -62,6 +62,8 @@ struct AttnParams {
     uint32_t k_batch_bcast, v_batch_bcast;  // K / V shared by every batch index (stride 0)
     float* out;             // f32 rows: depth contiguous, rows at the strides below
     uint64_t o_sb, o_sh, o_sl;              // output strides (elements) of batch, head, query
+    const void* mask;       // keep (u32) or additive (f32) mask, keys contiguous
+    uint64_t m_sb, m_sh, m_sq;              // mask strides (elements; 0 = broadcast) of batch, head, query
 };
 
 template <int D>
@@ -175,7 +177,10 @@ __device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t 
     return (uint32_t)(need < (int64_t)p.kv_tiles ? need : p.kv_tiles);
 }
 
-template <int D>
+// MASK: FB_MASK_NONE, FB_MASK_KEEP (u32, nonzero keeps the key) or
+// FB_MASK_ADDITIVE (f32 added to the scaled score; -inf excludes the key), as
+// the reference applies them (compute-cuda/src/attention.cu:55-80).
+template <int D, int MASK>
 __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV, AttnParams p) {
@@ -353,12 +358,36 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
             // tiles that reach them; logits are x * sl, so the row maximum of
             // the logits is the maximum of x (sl > 0) or its minimum (sl < 0).
             const int64_t key0 = (int64_t)j * TK;
-            const bool edge = key0 + TK > (int64_t)p.Lk || key0 + TK - 1 > vis;
+            const bool edge = MASK != FB_MASK_NONE || key0 + TK > (int64_t)p.Lk || key0 + TK - 1 > vis;
             if (edge || sl == 0.0f) {
                 const int64_t lim64 = min((int64_t)p.Lk - key0, vis - key0 + 1);
                 const int32_t lim = (int32_t)(lim64 < 0 ? 0 : (lim64 > TK ? TK : lim64));
+                if constexpr (MASK == FB_MASK_NONE) {
 #pragma unroll
-                for (int i = 0; i < TK; ++i) x[i] = i < lim ? x[i] * sl : NEG;  // logits, masked
+                    for (int i = 0; i < TK; ++i) x[i] = i < lim ? x[i] * sl : NEG;  // logits, masked
+                } else {
+                    // This row's mask values for the tile's keys, 16 bytes at a
+                    // time (keys contiguous; only keys < Lk of rows < L read).
+                    const uint64_t mrow = (uint64_t)batch * p.m_sb + (uint64_t)head * p.m_sh + (uint64_t)q * p.m_sq + key0;
+                    const bool row_ok = q < p.L;
+#pragma unroll
+                    for (int c = 0; c < TK / 4; ++c) {
+                        uint4 mv = make_uint4(0u, 0u, 0u, 0u);
+                        if (row_ok && c * 4 < lim)
+                            mv = *reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(p.mask) + mrow + c * 4);
+                        const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int i = c * 4 + e;
+                            if constexpr (MASK == FB_MASK_KEEP) {
+                                x[i] = (i < lim && row_ok && mw[e] != 0u) ? x[i] * sl : NEG;
+                            } else {
+                                const float bias = __uint_as_float(mw[e]);
+                                x[i] = (i < lim && row_ok && bias != NEG) ? fmaf(bias, 1.4426950408889634f, x[i] * sl) : NEG;
+                            }
+                        }
+                    }
+                }
             }
             const bool raw = !(edge || sl == 0.0f);
             const bool use_min = raw && sl < 0.0f;
@@ -552,7 +581,7 @@ bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t D, 
 
 template <int D>
 int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLayout& kl, const RowsLayout& vl,
-             const RowsLayout& ol, cudaStream_t st) {
+             const RowsLayout& ol, const RowsLayout& ml, cudaStream_t st) {
     using C = ACfg<D>;
     const int r = (int)a.row_rank;
     const uint64_t L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
@@ -588,7 +617,13 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     p.o_sb = ol.s_batch;
     p.o_sh = ol.s_head;
     p.o_sl = ol.s_row;
-    auto kernel = attn_fwd_kernel<D>;
+    p.mask = a.mask_kind == FB_MASK_NONE ? nullptr : static_cast<const uint32_t*>(a.mask) + a.m_offset;
+    p.m_sb = ml.s_batch;
+    p.m_sh = ml.s_head;
+    p.m_sq = ml.s_row;
+    auto kernel = a.mask_kind == FB_MASK_KEEP       ? attn_fwd_kernel<D, FB_MASK_KEEP>
+                  : a.mask_kind == FB_MASK_ADDITIVE ? attn_fwd_kernel<D, FB_MASK_ADDITIVE>
+                                                    : attn_fwd_kernel<D, FB_MASK_NONE>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return launch_status("shared-memory attribute");
     const uint64_t grid = (uint64_t)p.q_blocks * BH;
@@ -610,7 +645,6 @@ uint32_t read_attention_status() {
 
 int launch_attention_tc(const AttnArgs& a, void* stream) {
     if (a.dtype != FB_BF16 && a.dtype != FB_F16) return FB_ERR_UNSUPPORTED;
-    if (a.mask_kind != FB_MASK_NONE) return FB_ERR_UNSUPPORTED;
     if (a.depth != a.value_depth || (a.depth != 64 && a.depth != 128)) return FB_ERR_UNSUPPORTED;
     if (a.row_rank < 2 || a.keys == 0 || a.rows == 0) return FB_ERR_UNSUPPORTED;
     const int r = (int)a.row_rank;
@@ -635,6 +669,17 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
     // f32 output rows take float4 stores: 16-byte aligned rows
     auto mult4 = [](uint64_t s, uint64_t n) { return n <= 1 || s % 4 == 0; };
     if (!mult4(ol.s_row, L) || !mult4(ol.s_head, H) || !mult4(ol.s_batch, ol.batch)) return FB_ERR_UNSUPPORTED;
+    // Masks (32-bit elements) are read 16 bytes at a time along contiguous
+    // keys; rows start 16-byte aligned.  Broadcast axes have stride 0.
+    RowsLayout ml;
+    if (a.mask_kind != FB_MASK_NONE) {
+        if (a.m_stride_key != 1 || Lk % 4 != 0) return FB_ERR_UNSUPPORTED;
+        ml.rows = L, ml.heads = H, ml.s_row = a.m_row_strides[r - 1], ml.s_head = a.m_row_strides[r - 2];
+        if (!merge_batch(a, a.m_row_strides, r - 2, &ml)) return FB_ERR_UNSUPPORTED;
+        if (!ml.batch_bcast && ml.batch != ql.batch) return FB_ERR_UNSUPPORTED;
+        if (ml.s_row % 4 != 0 || ml.s_head % 4 != 0 || ml.s_batch % 4 != 0) return FB_ERR_UNSUPPORTED;
+        if ((reinterpret_cast<uintptr_t>(a.mask) + a.m_offset * 4) % 16 != 0) return FB_ERR_UNSUPPORTED;
+    }
     auto aligned = [](const void* p, uint64_t off, uint64_t esz) {
         return (reinterpret_cast<uintptr_t>(p) + off * esz) % 16 == 0;
     };
@@ -643,7 +688,7 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
         return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return D == 64 ? launch_d<64>(a, fmt, ql, kl, vl, ol, st) : launch_d<128>(a, fmt, ql, kl, vl, ol, st);
+    return D == 64 ? launch_d<64>(a, fmt, ql, kl, vl, ol, ml, st) : launch_d<128>(a, fmt, ql, kl, vl, ol, ml, st);
 }
 
 }  // namespace fb

@@ -120,3 +120,43 @@ def test_tc_attention_broadcast_kv_batch(cuda):
     k = torch.randn(1, 2, 192, 64, generator=g).bfloat16().to(cuda).expand(3, 2, 192, 64)
     v = torch.randn(1, 2, 192, 64, generator=g).bfloat16().to(cuda).expand(3, 2, 192, 64)
     _check_views(cuda, q, k, v, causal=0)
+
+
+def _masked_case(cuda, kind, qs, ks, mshape, causal=None, seed=41):
+    from forma_b200.api import Mask
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(*qs, generator=g).bfloat16()
+    k = torch.randn(*ks, generator=g).bfloat16()
+    v = torch.randn(*ks, generator=g).bfloat16()
+    if kind == "keep":
+        keep = (torch.rand(*mshape, generator=g) > 0.3).to(torch.int32)
+        keep[..., 0, :] = 0  # a fully masked query row -> zeros
+        mask = Mask("keep", keep.to(cuda))
+        additive = np.where(keep.numpy() != 0, 0.0, -np.inf)
+    else:
+        add = torch.randn(*mshape, generator=g) * 2
+        add[torch.rand(*mshape, generator=g) < 0.2] = float("-inf")
+        mask = Mask("additive", add.to(cuda))
+        additive = add.numpy().astype(np.float64)
+    before = api.launch_count()
+    got = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), mask, AttentionOptions(None, causal)).cpu().numpy()
+    assert api.device_status() == 0
+    assert api.launch_count() > before
+    ref = orc.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), additive, None, causal,
+                        nthreads=orc.threads())
+    assert np.isfinite(got).all()
+    err = float(np.abs(got.astype(np.float64) - ref).max()) / max(float(np.abs(ref).max()), 1e-30)
+    assert err <= 2e-2, err
+    return got, ref
+
+
+def test_tc_attention_keep_mask_broadcast(cuda):
+    # [L, Lk] keep mask broadcast over batch and heads; a fully masked row
+    got, ref = _masked_case(cuda, "keep", (2, 3, 256, 64), (2, 3, 320, 64), (256, 320))
+    assert np.abs(got[:, :, 0]).max() == 0.0
+
+
+def test_tc_attention_additive_mask_per_head_causal(cuda):
+    # additive mask with -inf entries, per head (broadcast over batch), causal, D = 128
+    _masked_case(cuda, "additive", (2, 2, 256, 128), (2, 2, 256, 128), (1, 2, 256, 256), causal=0)
