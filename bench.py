@@ -344,7 +344,13 @@ def run_ops(api, dev, dist, args, pk) -> dict:
            "random-init pre-norm encoder, LN eps 1e-5, tanh GELU; FLOPs = patch conv + per layer QKV/out/MLP "
            "projections (1x1 convs) + attention 4*B*H*L^2*D; glue (casts, adds, LN) counted as time only")
     res["vit_encoder_c5"]["flops_by_stage"] = fl
-    del enc, img
+    # the same forward as a prepared program (one CUDA graph launch per forward)
+    from forma_b200.program import Program
+
+    prog = Program(enc.forward, img, device=dev)
+    record("vit_encoder_c5_graph", prog.run, fl["total"], pk["bf16_tflops"], "measured bf16 dense (burst)",
+           "the C5 forward captured once and replayed as one CUDA graph (forma_b200.program.Program)")
+    del prog, enc, img
     return res
 
 

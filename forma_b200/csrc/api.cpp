@@ -513,6 +513,14 @@ void* scratch(void* stream, uint64_t bytes, int slot) {
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     ScratchBlock& b = g_scratch[std::make_tuple(dev, stream, slot)];
     if (b.bytes >= bytes) return b.ptr;
+    // No allocation while the stream is being captured into a graph (it would
+    // invalidate the capture): an eager call on the stream must come first.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cap) == cudaSuccess &&
+        cap != cudaStreamCaptureStatusNone) {
+        g_driver_error = "library scratch must be allocated by an eager call on this stream before graph capture";
+        return nullptr;
+    }
     // Growing: the old block may still be read by enqueued work on this
     // stream, so it is kept (leaked) rather than freed under the stream.
     uint64_t want = std::max<uint64_t>(bytes, b.bytes * 2);
