@@ -333,6 +333,13 @@ def run_ops(api, dev, dist, args, pk) -> dict:
            4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
            "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2")
     del q, k, v
+    # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32 output
+    a = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
+    b = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
+    c = torch.empty(8192, 8192, device=dev)
+    record("matmul_bf16_8192", lambda: api.matmul_low_f32(a, b, out=c), 2 * 8192 ** 3, pk["bf16_tflops"],
+           "measured bf16 dense (burst)", "row-major right operand (MN-major B); f32 output")
+    del a, b, c
     # C5: ViT-style encoder forward, [64,3,224,224] bf16, patch 16, 12 layers (E 768, H 12, D 64, L 197, MLP 3072)
     from forma_b200.vit import ViTConfig, ViTEncoder
 

@@ -31,6 +31,8 @@ STATUS_NAMES = {
     11: "InvalidAttentionScale",
     12: "InvalidConvolution",
     13: "LowDtypeMismatch",
+    14: "MatmulRank",
+    15: "MatmulInnerDimension",
     32: "InvalidInput",
     33: "Dtype",
     34: "Driver",
@@ -110,6 +112,9 @@ SIGNATURES = {
     "fb_moments": (C.c_int, [T, U32P, C.c_uint32, C.c_int32, T, T, VP]),
     "fb_layer_norm": (C.c_int, [T, U32P, C.c_uint32, C.c_float, T, VP]),
     "fb_cast_to_low": (C.c_int, [T, T, VP]),
+    "fb_matmul_plan": (C.c_int, [U64P, C.c_uint32, U64P, C.c_uint32, U64P, U32P]),
+    "fb_matmul_low_f32": (C.c_int, [T, T, T, VP]),
+    "fb_matmul_low": (C.c_int, [T, T, T, VP]),
     "fb_add": (C.c_int, [T, T, T, VP]),
     "fb_gelu_to_low": (C.c_int, [T, T, VP]),
 }

@@ -242,6 +242,36 @@ def conv_low_into(input, weight, options, out):
     return out
 
 
+# ------------------------------------------------------- low-precision GEMM
+
+def matmul_plan(left_shape: Sequence[int], right_shape: Sequence[int]) -> list:
+    """MatmulPlan::new output dims (host only)."""
+    out = (C.c_uint64 * _lib.MAX_RANK)()
+    rank = C.c_uint32()
+    _check(lib().fb_matmul_plan(_lib.u64_array(left_shape), len(left_shape), _lib.u64_array(right_shape),
+                                len(right_shape), out, C.byref(rank)))
+    return [out[i] for i in range(rank.value)]
+
+
+def _matmul(fn, left, right, out_dtype, out=None):
+    dev = _device(left, right)
+    if out is None:
+        out = torch.empty(matmul_plan(list(left.shape), list(right.shape)), dtype=out_dtype, device=dev)
+    dl, dr, do = describe(left), describe(right), describe(out)
+    _check(fn(C.byref(dl), C.byref(dr), C.byref(do), _stream(dev)))
+    return out
+
+
+def matmul_low_f32(left: torch.Tensor, right: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """f16/bf16 operands (one dtype), f32 accumulation and output; vectors and batches broadcast."""
+    return _matmul(lib().fb_matmul_low_f32, left, right, torch.float32, out)
+
+
+def matmul_low(left: torch.Tensor, right: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """matmul_low_f32 rounded once (nearest even) to the operands' dtype."""
+    return _matmul(lib().fb_matmul_low, left, right, left.dtype, out)
+
+
 # ------------------------------------------------------------- attention
 
 def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions, out=None):

@@ -481,6 +481,105 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     return launched(s, "attention");
 }
 
+// MatmulPlan::new (tensor-core/src/shape.rs:148-192).
+struct MatmulPlanH {
+    Dims left, right;      // vector operands promoted to matrices
+    Dims matrix_output;    // batch..., M, N
+    Dims output;           // promoted axes removed again
+    bool left_vector = false, right_vector = false;
+};
+
+Error matmul_plan(const Dims& left, const Dims& right, MatmulPlanH* p) {
+    if (left.empty() || right.empty())
+        return err(FB_ERR_MATMUL_RANK, "matmul operands need rank >= 1 (left rank " + std::to_string(left.size()) +
+                                           ", right rank " + std::to_string(right.size()) + ")");
+    p->left_vector = left.size() == 1;
+    p->right_vector = right.size() == 1;
+    p->left = p->left_vector ? Dims{1, left[0]} : left;
+    p->right = p->right_vector ? Dims{right[0], 1} : right;
+    const Dims& a = p->left;
+    const Dims& b = p->right;
+    if (a[a.size() - 1] != b[b.size() - 2])
+        return err(FB_ERR_MATMUL_INNER_DIMENSION, "matmul inner dimensions differ: " + std::to_string(a[a.size() - 1]) +
+                                                      " vs " + std::to_string(b[b.size() - 2]));
+    Dims batch;
+    Error e = broadcast_dims(Dims(a.begin(), a.end() - 2), Dims(b.begin(), b.end() - 2), &batch);
+    if (!ok(e)) return e;
+    p->matrix_output = batch;
+    p->matrix_output.push_back(a[a.size() - 2]);
+    p->matrix_output.push_back(b[b.size() - 1]);
+    p->output = p->matrix_output;
+    if (p->right_vector) p->output.pop_back();
+    if (p->left_vector) p->output.erase(p->output.end() - (p->right_vector ? 1 : 2));
+    uint64_t n;
+    return numel(p->output, &n);
+}
+
+int matmul_impl(const fb_tensor* left, const fb_tensor* right, fb_tensor* output, void* stream, bool round_low) {
+    View l, r, out;
+    FB_TRY(view_of(left, "left", &l));
+    FB_TRY(view_of(right, "right", &r));
+    if (!is_low(l.dtype) || !is_low(r.dtype)) return fail(FB_ERR_DTYPE, "low GEMM operands must be f16 or bf16");
+    if (l.dtype != r.dtype) return fail(FB_ERR_INVALID_INPUT, "low GEMM inputs must have the same dtype");
+    MatmulPlanH plan;
+    FB_TRY(matmul_plan(l.dims, r.dims, &plan));
+    FB_TRY(check_output(output, "output", plan.output, round_low ? l.dtype : FB_F32, &out));
+    if (out.count == 0) return FB_OK;
+    // promoted operand strides (a promoted unit axis has stride 0)
+    Dims ls = l.strides, rs = r.strides;
+    if (plan.left_vector) ls.insert(ls.begin(), 0);
+    if (plan.right_vector) rs.push_back(0);
+    const Dims& ld = plan.left;
+    const Dims& rd = plan.right;
+    const size_t nb = plan.matrix_output.size() - 2;
+    // output strides in matrix_output form (removed vector axes: stride 0)
+    Dims os(plan.matrix_output.size(), 0);
+    {
+        size_t j = 0;
+        for (size_t i = 0; i < nb; ++i) os[i] = out.strides[j++];
+        os[nb] = plan.left_vector ? 0 : out.strides[j++];
+        os[nb + 1] = plan.right_vector ? 0 : out.strides[j++];
+    }
+    GemmArgs g;
+    g.a = l.data;
+    g.b = r.data;
+    g.out = out.data;
+    g.dtype = l.dtype;
+    g.out_low = round_low ? out.dtype : 0;
+    g.M = ld[ld.size() - 2];
+    g.K = ld[ld.size() - 1];
+    g.N = rd[rd.size() - 1];
+    g.a_off = l.offset;
+    g.b_off = r.offset;
+    g.o_off = out.offset;
+    g.a_sm = ls[ls.size() - 2];
+    g.a_sk = ls[ls.size() - 1];
+    g.b_sk = rs[rs.size() - 2];
+    g.b_sn = rs[rs.size() - 1];
+    g.o_sm = os[nb];
+    g.o_sn = os[nb + 1];
+    // batch nests over the broadcast batch axes, operands right-aligned
+    Dims bdims(plan.matrix_output.begin(), plan.matrix_output.begin() + nb);
+    auto batch_strides = [&](const Dims& d, const Dims& st) {
+        Dims s(nb, 0);
+        const size_t ob = d.size() - 2;
+        for (size_t i = 0; i < nb; ++i) {
+            if (i + ob < nb) continue;
+            const size_t j = i + ob - nb;
+            s[i] = d[j] == 1 ? 0 : st[j];
+        }
+        return s;
+    };
+    Dims ob(os.begin(), os.begin() + nb);
+    g.a_batch = make_nest(bdims, batch_strides(ld, ls), all_axes(nb));
+    g.b_batch = make_nest(bdims, batch_strides(rd, rs), all_axes(nb));
+    g.o_batch = make_nest(bdims, ob, all_axes(nb));
+    FB_TRY(numel(bdims, &g.batch));
+    int st = launch_gemm_tc(g, stream);
+    if (st == FB_ERR_UNSUPPORTED) st = launch_gemm_simt(g, stream);
+    return launched(st, "matmul");
+}
+
 }  // namespace
 
 // ------------------------------------------------------------ scratch
@@ -557,6 +656,8 @@ const char* fb_status_string(int status) {
         case FB_ERR_INVALID_CONVOLUTION: return "invalid convolution";
         case FB_ERR_LOW_DTYPE_MISMATCH: return "low-precision dtypes must match";
         case FB_ERR_INVALID_INPUT: return "invalid input";
+        case FB_ERR_MATMUL_RANK: return "matmul operands need rank >= 1";
+        case FB_ERR_MATMUL_INNER_DIMENSION: return "matmul inner dimensions differ";
         case FB_ERR_DTYPE: return "tensor dtype mismatch";
         case FB_ERR_DRIVER: return "CUDA driver error";
         case FB_ERR_UNSUPPORTED: return "unsupported";
@@ -583,6 +684,26 @@ int fb_conv_plan(const uint64_t* input_dims, uint32_t input_rank, const uint64_t
     *out_rank = (uint32_t)plan.output.size();
     std::copy(plan.output.begin(), plan.output.end(), out_dims);
     return FB_OK;
+}
+
+int fb_matmul_plan(const uint64_t* left_dims, uint32_t left_rank, const uint64_t* right_dims, uint32_t right_rank,
+                   uint64_t* out_dims, uint32_t* out_rank) {
+    if (left_rank > FB_MAX_RANK || right_rank > FB_MAX_RANK || !out_dims || !out_rank)
+        return fail(FB_ERR_INVALID_INPUT, "invalid plan arguments");
+    MatmulPlanH plan;
+    FB_TRY(matmul_plan(Dims(left_dims, left_dims + left_rank), Dims(right_dims, right_dims + right_rank), &plan));
+    if (plan.output.size() > FB_MAX_RANK) return fail(FB_ERR_INVALID_INPUT, "matmul output rank too large");
+    *out_rank = (uint32_t)plan.output.size();
+    std::copy(plan.output.begin(), plan.output.end(), out_dims);
+    return FB_OK;
+}
+
+int fb_matmul_low_f32(const fb_tensor* left, const fb_tensor* right, fb_tensor* output, void* stream) {
+    return matmul_impl(left, right, output, stream, false);
+}
+
+int fb_matmul_low(const fb_tensor* left, const fb_tensor* right, fb_tensor* output, void* stream) {
+    return matmul_impl(left, right, output, stream, true);
 }
 
 int fb_conv(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,

@@ -155,17 +155,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
-// Shared-memory descriptor of an MN-major, 128B-swizzled operand: 64-element
-// rows along N, 8-row (K) atoms 1024 B apart, N blocks of 64 `lbo` bytes apart.
-__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t smem_addr, uint32_t lbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)(1024u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
-}
 
 // Key tiles visible to the 128 query rows starting at q0 (0 if none exist).
 __device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t q0) {

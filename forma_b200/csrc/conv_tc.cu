@@ -45,6 +45,7 @@ struct ConvGemmParams {
     int32_t pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
     uint32_t m_tiles, n_tiles;
     uint32_t c_rows;  // 1: channels contiguous (s_c == 1) and aligned rows (16 B for f32, 8 B for 16-bit)
+    uint32_t b_mn;    // 0: B map is [N, K] (K contiguous); 1: B map is [K, N] (N contiguous, MN-major operand)
     uint32_t out_low; // 0: f32 output; FB_BF16 / FB_F16: rounded once (nearest even) to that type
     float* out;       // f32 output, or the 16-bit output's storage when out_low != 0
     uint64_t out_offset, s_n, s_c, s_p, s_q;
@@ -135,7 +136,15 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                     tma_load_im2col_4d(a_dst, &tmA, (int32_t)(cb * BK), w0, h0, n0, (uint16_t)(s * p.dil_w),
                                        (uint16_t)(r * p.dil_h), &full[stage]);
                 }
-                tma_load_2d(b_dst, &tmB, (int32_t)(kb * BK), (int32_t)(nt * BN), &full[stage]);
+                if (p.b_mn) {
+                    // [K, N] rows: BN / 64 boxes of 64 k-rows x 64 columns (8 KB each)
+#pragma unroll
+                    for (int nb = 0; nb < BN / 64; ++nb)
+                        tma_load_2d(b_dst + nb * (BK * 128), &tmB, (int32_t)(nt * BN + nb * 64), (int32_t)(kb * BK),
+                                    &full[stage]);
+                } else {
+                    tma_load_2d(b_dst, &tmB, (int32_t)(kb * BK), (int32_t)(nt * BN), &full[stage]);
+                }
                 ++issued;
                 if (++stage == C::STAGES) {
                     stage = 0;
@@ -160,6 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
         // The whole warp runs the loop with warp-uniform operands and waits;
         // one elected lane issues each tcgen05.mma / commit.
         const uint32_t idesc = f16_idesc(p.fmt, BM, BN);
+        const uint32_t idesc_mn = idesc | (1u << 16);  // B MN-major
         auto wait = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
         uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
         bool failed = false;
@@ -177,10 +187,20 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                 }
                 tc_fence_after();
                 const uint64_t ad = sw128_desc(smem_u32(ring + stage * C::STAGE_BYTES));
-                const uint64_t bd = desc_add(ad, C::A_BYTES);
-                umma_f16_ss_warp(d, ad, bd, idesc, kb != 0);
+                if (p.b_mn) {
+                    // MN-major B: 64-column blocks BK * 128 bytes apart, 16 k-rows per step
+                    const uint64_t bd = sw128_mn_desc(smem_u32(ring + stage * C::STAGE_BYTES + C::A_BYTES), BK * 128);
+                    umma_f16_ss_warp(d, ad, bd, idesc_mn, kb != 0);
 #pragma unroll
-                for (int k = 1; k < BK / 16; ++k) umma_f16_ss_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 32), idesc, 1u);
+                    for (int k = 1; k < BK / 16; ++k)
+                        umma_f16_ss_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 16 * 128), idesc_mn, 1u);
+                } else {
+                    const uint64_t bd = desc_add(ad, C::A_BYTES);
+                    umma_f16_ss_warp(d, ad, bd, idesc, kb != 0);
+#pragma unroll
+                    for (int k = 1; k < BK / 16; ++k)
+                        umma_f16_ss_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 32), idesc, 1u);
+                }
                 umma_commit_warp(&empty[stage]);  // frees the stage when these MMAs complete
                 if (++stage == C::STAGES) {
                     stage = 0;
@@ -436,6 +456,72 @@ bool c_rows_ok(const ConvArgs& a) {
         if (st % 4 != 0) return false;
     const uint64_t esz = a.out_low ? 2 : 4;
     return (reinterpret_cast<uintptr_t>(a.output) + a.out_offset * esz) % (4 * esz) == 0;
+}
+
+// Element offset of a batch index in a batch nest (row-major).
+uint64_t host_nest_offset(const Nest& n, uint64_t linear) {
+    uint64_t off = 0;
+    for (int d = (int)n.rank - 1; d >= 0; --d) {
+        off += (linear % n.dims[d]) * n.strides[d];
+        linear /= n.dims[d];
+    }
+    return off;
+}
+
+// Low-precision GEMM on the implicit-GEMM kernel: A = left rows [M, K] (K
+// contiguous), B = right as [K, N] rows (N contiguous: MN-major operand) or
+// [N, K] rows (K contiguous), one launch per batch index.
+int launch_gemm_tc(const GemmArgs& g, void* stream) {
+    if (g.dtype != FB_BF16 && g.dtype != FB_F16) return FB_ERR_UNSUPPORTED;
+    if (g.M == 0 || g.N == 0 || g.K == 0 || g.K % BK != 0 || g.M > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
+    const int BN = g.N % 256 == 0 ? 256 : g.N % 128 == 0 ? 128 : g.N % 64 == 0 ? 64 : 0;
+    if (BN == 0) return FB_ERR_UNSUPPORTED;
+    if (g.a_sk != 1 || g.a_sm % 8 != 0 || g.a_sm < g.K) return FB_ERR_UNSUPPORTED;
+    const bool b_mn = g.b_sn == 1 && g.b_sk % 8 == 0 && g.b_sk >= g.N;
+    const bool b_k = !b_mn && g.b_sk == 1 && g.b_sn % 8 == 0 && g.b_sn >= g.K;
+    if (!b_mn && !b_k) return FB_ERR_UNSUPPORTED;
+    const uint64_t esz_out = g.out_low ? 2 : 4;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t fmt = g.dtype == FB_BF16 ? 1 : 0;
+    for (uint64_t bi = 0; bi < g.batch; ++bi) {
+        const uint16_t* a = static_cast<const uint16_t*>(g.a) + g.a_off + host_nest_offset(g.a_batch, bi);
+        const uint16_t* b = static_cast<const uint16_t*>(g.b) + g.b_off + host_nest_offset(g.b_batch, bi);
+        const uint64_t o_off = g.o_off + host_nest_offset(g.o_batch, bi);
+        if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(b) % 16 != 0) return FB_ERR_UNSUPPORTED;
+        CUtensorMap ta, tb;
+        if (!make_2d_map(&ta, a, fmt, g.K, g.M, g.a_sm, BM)) return FB_ERR_UNSUPPORTED;
+        if (b_mn ? !make_2d_map(&tb, b, fmt, g.N, g.K, g.b_sk, BK) : !make_2d_map(&tb, b, fmt, g.K, g.N, g.b_sn, (uint32_t)BN))
+            return FB_ERR_UNSUPPORTED;
+        ConvGemmParams p{};
+        p.mode = 0;
+        p.fmt = fmt;
+        p.M = (uint32_t)g.M;
+        p.P = 1;
+        p.Q = (uint32_t)g.M;
+        p.c_blocks = p.k_blocks = (uint32_t)(g.K / BK);
+        p.S = 1;
+        p.stride_h = p.stride_w = p.dil_h = p.dil_w = 1;
+        p.m_tiles = (uint32_t)((g.M + BM - 1) / BM);
+        p.n_tiles = (uint32_t)(g.N / BN);
+        p.out = static_cast<float*>(g.out);
+        p.out_offset = o_off;
+        p.s_n = 0;
+        p.s_p = 0;
+        p.s_q = g.o_sm;
+        p.s_c = g.o_sn;
+        p.out_low = g.out_low;
+        p.b_mn = b_mn ? 1 : 0;
+        p.c_rows = g.o_sn == 1 && g.o_sm % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(g.out) + o_off * esz_out) % (4 * esz_out) == 0;
+        int r;
+        switch (BN) {
+            case 256: r = launch_bn<256>(ta, tb, p, st); break;
+            case 128: r = launch_bn<128>(ta, tb, p, st); break;
+            default: r = launch_bn<64>(ta, tb, p, st); break;
+        }
+        if (r != FB_OK) return r;
+    }
+    return FB_OK;
 }
 
 int launch_patches(const ConvArgs& a, void* stream) {

@@ -153,6 +153,23 @@ int launch_conv_direct(const ConvArgs& a, void* stream);
 int launch_conv2d_f32_tiled(const ConvArgs& a, void* stream);
 int launch_conv_tc(const ConvArgs& a, void* stream);
 
+// ---- low-precision GEMM (conv_tc.cu tensor cores, gemm_simt.cu any layout) ----
+struct GemmArgs {
+    const void* a = nullptr;  // left  [batch..., M, K]
+    const void* b = nullptr;  // right [batch..., K, N]
+    void* out = nullptr;      // [batch..., M, N]
+    uint32_t dtype = FB_BF16; // operands
+    uint32_t out_low = 0;     // 0: f32 output; FB_BF16 / FB_F16: rounded once
+    uint64_t M = 0, N = 0, K = 0;
+    uint64_t a_off = 0, b_off = 0, o_off = 0;
+    uint64_t a_sm = 0, a_sk = 0, b_sk = 0, b_sn = 0, o_sm = 0, o_sn = 0;  // element strides
+    uint64_t batch = 1;                 // batch index count
+    Nest a_batch, b_batch, o_batch;     // batch index -> element offset (stride 0 broadcasts)
+};
+// Returns FB_ERR_UNSUPPORTED when the layout or sizes have no tensor-core form.
+int launch_gemm_tc(const GemmArgs& g, void* stream);
+int launch_gemm_simt(const GemmArgs& g, void* stream);
+
 // ---- attention (attention_simt.cu, attention_tc.cu) ----
 struct AttnArgs {
     const void* q = nullptr;

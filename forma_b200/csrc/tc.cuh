@@ -51,6 +51,18 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory descriptor of an MN-major, 128B-swizzled operand: 64-element
+// rows along N, 8-row (K) atoms 1024 B apart, N blocks of 64 `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
 // Instruction descriptor of kind::f16: f32 accumulate, A and B of one 16-bit
 // type (fmt 0 = f16, 1 = bf16), both K-major, M x N.
 __host__ __device__ constexpr uint32_t f16_idesc(uint32_t fmt, uint32_t m, uint32_t n) {

@@ -61,6 +61,8 @@ typedef enum fb_status {
     FB_ERR_INVALID_ATTENTION_SCALE = 11,
     FB_ERR_INVALID_CONVOLUTION = 12,
     FB_ERR_LOW_DTYPE_MISMATCH = 13,
+    FB_ERR_MATMUL_RANK = 14,
+    FB_ERR_MATMUL_INNER_DIMENSION = 15,
     FB_ERR_INVALID_INPUT = 32,
     FB_ERR_DTYPE = 33,
     FB_ERR_DRIVER = 34,
@@ -291,6 +293,27 @@ int fb_layer_norm(const fb_tensor* input, const uint32_t* axes,
  * encode_low at compute-cuda/src/low_precision.cu:6-16): nearest-even f32 ->
  * F16/BF16 of `output->dtype`; `output` must be contiguous. */
 int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream);
+
+/* ------------------------------------------------------ low-precision GEMM */
+
+/* MatmulPlan::new (tensor-core/src/shape.rs:141-192): vectors are promoted
+ * (left [K] -> [1, K], right [K] -> [K, 1]) and removed again from the output,
+ * batch axes broadcast.  Writes the output dims. */
+int fb_matmul_plan(const uint64_t* left_dims, uint32_t left_rank,
+                   const uint64_t* right_dims, uint32_t right_rank,
+                   uint64_t* out_dims, uint32_t* out_rank);
+
+/* TensorLowBackend::matmul_low_f32 / matmul_low (tensor-core/src/
+ * low_precision.rs:96-106; replaces the cuBLAS GEMM of compute-cuda/src/
+ * low_precision.rs:240-270 and matmul.rs:144-162): f16/bf16 operands of one
+ * dtype, f32 accumulation; matmul_low_f32 writes f32, matmul_low rounds the
+ * f32 result once (nearest even) to the operands' dtype.  Any strides; the
+ * tensor cores take rows with a contiguous K axis on the left and either a
+ * contiguous N or K axis on the right (K and N multiples of 64). */
+int fb_matmul_low_f32(const fb_tensor* left, const fb_tensor* right,
+                      fb_tensor* output, void* stream);
+int fb_matmul_low(const fb_tensor* left, const fb_tensor* right,
+                  fb_tensor* output, void* stream);
 
 /* ------------------------------------------------------- elementwise glue */
 

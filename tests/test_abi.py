@@ -207,3 +207,20 @@ def test_validation_precedes_any_launch():
     assert lib.fb_reduce_f32(0, C.byref(x), ax, 1, 0, C.byref(y), None) == 32
     # status strings
     assert lib.fb_status_string(8).decode().startswith("min, max and mean")
+
+
+def test_matmul_plan_follows_reference_shapes():
+    # MatmulPlan::new (tensor-core/src/shape.rs:148-192): promotion and broadcast
+    assert api.matmul_plan([3], [3]) == []
+    assert api.matmul_plan([2, 3], [3]) == [2]
+    assert api.matmul_plan([3], [3, 4]) == [4]
+    assert api.matmul_plan([5, 1, 2, 3], [4, 3, 6]) == [5, 4, 2, 6]
+    with pytest.raises(api.TensorError) as e:
+        api.matmul_plan([], [3])
+    assert e.value.kind == "MatmulRank"
+    with pytest.raises(api.TensorError) as e:
+        api.matmul_plan([2, 3], [4, 5])
+    assert e.value.kind == "MatmulInnerDimension"
+    with pytest.raises(api.TensorError) as e:
+        api.matmul_plan([2, 2, 3], [3, 3, 4])
+    assert e.value.kind == "IncompatibleBroadcast"
