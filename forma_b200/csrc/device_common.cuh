@@ -104,6 +104,24 @@ __device__ __forceinline__ double warp_sum(double v) {
     for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
     return v;
 }
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    return v;
+}
+// Three-input maximum that ignores NaN operands (NaN only when all are NaN).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error about
+// 2^-22; subnormal results flush to zero; -inf -> 0, NaN -> NaN).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int d = 16; d; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));

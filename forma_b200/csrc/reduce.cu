@@ -295,10 +295,17 @@ __device__ __forceinline__ float4 smem_load4(const unsigned char* row, uint64_t 
 // Operation codes of the streamed engine: RowOp values, then StatsOp + 16.
 constexpr uint32_t STREAM_STATS = 16;
 
+// Operation families, one kernel instantiation each, so that every family
+// gets the registers (and so the blocks per SM) that its own code needs.
+constexpr int FAM_SUM = 0;      // sum, mean
+constexpr int FAM_EXTREME = 1;  // min, max, argmax
+constexpr int FAM_EXP = 2;      // softmax, log-softmax, logsumexp
+constexpr int FAM_MOMENTS = 3;  // moments, layer norm
+
 // CAP: registers capped so that six 128-thread blocks fit per SM (argmax and
 // moments hold more per-row state and measured faster with the extra blocks;
 // the light reductions measured faster uncapped).
-template <typename T, int NV, int TB, bool CAP>
+template <typename T, int NV, int TB, bool CAP, int FAM>
 __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
                                                             float eps, uint32_t stages, uint32_t row_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -309,12 +316,14 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
     // every thread has passed the next row's first barrier).
     __shared__ double s_d[2][2][TB / 32];
     __shared__ float s_f[2][TB / 32];
+    __shared__ float s_e[2][TB / 32];
     __shared__ uint64_t s_k[2][TB / 32];
     __shared__ int s_abort;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint64_t first = blockIdx.x, step = gridDim.x;
     const uint64_t mine = first < in.rows ? (in.rows - 1 - first) / step + 1 : 0;
     const uint64_t n = in.cols;
+    const double inv_n = 1.0 / (double)n;  // one division per thread, not per row
     const T* base = reinterpret_cast<const T*>(in.data) + in.offset;
     if (tid == 0) {
         for (uint32_t s = 0; s < stages; ++s) mbar_init(&full[s], 1);
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
         };
         auto valid = [&](int j) { return (tid + (uint64_t)j * TB) * 4 < n; };
 
-        if (op == ROW_SUM || op == ROW_MEAN) {
+        if constexpr (FAM == FAM_SUM) {
             double a = 0.0;
 #pragma unroll
             for (int j = 0; j < NV; ++j)
@@ -368,7 +377,7 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 for (int w = 0; w < TB / 32; ++w) t += s_d[0][par][w];
                 static_cast<float*>(oa.data)[out_index(oa, row)] = op == ROW_MEAN ? (float)(t / (double)n) : (float)t;
             }
-        } else if (op == ROW_MIN || op == ROW_MAX || op == ROW_ARGMAX) {
+        } else if constexpr (FAM == FAM_EXTREME) {
             // Keys in column order per thread: a strictly greater key wins,
             // so each thread keeps its lowest column among equal keys.
             const uint32_t flip = op == ROW_MIN ? 0xffffffffu : 0u;
@@ -438,12 +447,17 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 else
                     static_cast<float*>(oa.data)[out_index(oa, row)] = key_value(k);
             }
-        } else if (op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
-                   op == STREAM_STATS + STATS_LOGSUMEXP) {
+        } else if constexpr (FAM == FAM_EXP) {
+            // Row maximum (NaN operands ignored, as a NaN reaches every output
+            // through the sum anyway), then exp(x - max) once per element as
+            // 2^((x - max) log2 e) on the special-function unit, summed in f32
+            // (all terms positive: relative error below 2^-19 for 4096
+            // columns).  The reference takes expf of the f32 difference and
+            // sums in f64 (statistics.cu:37-45, 89-91).
             float m = -__int_as_float(0x7f800000);
 #pragma unroll
             for (int j = 0; j < NV; ++j)
-                if (valid(j)) m = fmaxf(m, fmaxf(fmaxf(c[j].x, c[j].y), fmaxf(c[j].z, c[j].w)));
+                if (valid(j)) m = max3(max3(m, c[j].x, c[j].y), c[j].z, c[j].w);
             m = warp_max(m);
             if (lane == 0) s_f[par][warp] = m;
             barrier_release();
@@ -454,43 +468,44 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
             m = s_f[par][0];
 #pragma unroll
             for (int w = 1; w < TB / 32; ++w) m = fmaxf(m, s_f[par][w]);
-            // exp(x - max) once per element (kept in registers for softmax);
-            // each thread's terms are summed in f32, threads combine in f64.
+            constexpr float kLog2e = 1.4426950408889634f;
             float e = 0.0f;
             const bool keep = op == STREAM_STATS + STATS_SOFTMAX;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 if (!valid(j)) continue;
                 const float4 x = c[j];
-                const float4 ex = make_float4(expf(x.x - m), expf(x.y - m), expf(x.z - m), expf(x.w - m));
+                const float4 ex = make_float4(ex2_approx((x.x - m) * kLog2e), ex2_approx((x.y - m) * kLog2e),
+                                              ex2_approx((x.z - m) * kLog2e), ex2_approx((x.w - m) * kLog2e));
                 e += (ex.x + ex.y) + (ex.z + ex.w);
                 if (keep) c[j] = ex;
             }
-            double ed = warp_sum((double)e);
-            if (lane == 0) s_d[1][par][warp] = ed;
+            e = warp_sum_f(e);
+            if (lane == 0) s_e[par][warp] = e;
             __syncthreads();
-            ed = 0.0;
+            e = 0.0f;
 #pragma unroll
-            for (int w = 0; w < TB / 32; ++w) ed += s_d[1][par][w];
+            for (int w = 0; w < TB / 32; ++w) e += s_e[par][w];
             if (op == STREAM_STATS + STATS_SOFTMAX) {
-                const float inv = (float)(1.0 / ed);
+                const float inv = __frcp_rn(e);
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
                         store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
                                    make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv));
             } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
-                const double ls = log(ed);
-                auto lsm = [&](float x) { return (float)(((double)x - (double)m) - ls); };
+                // (x - max) - log(sum): both terms within an f32 ulp
+                const float ls = logf(e);
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
                     if (valid(j))
                         store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
-                                   make_float4(lsm(c[j].x), lsm(c[j].y), lsm(c[j].z), lsm(c[j].w)));
+                                   make_float4((c[j].x - m) - ls, (c[j].y - m) - ls, (c[j].z - m) - ls,
+                                               (c[j].w - m) - ls));
             } else if (tid == 0) {
-                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log(ed));
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log((double)e));
             }
-        } else {
+        } else {  // FAM_MOMENTS
             // Moments / layer norm in one pass and one block reduction.  Each
             // thread sums, per float4, x (pairwise f32, f64 across float4s) and
             // (x - a)^2 around an anchor
@@ -548,17 +563,24 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 S += s_d[0][par][w];
                 Q += s_d[1][par][w];
             }
+            // Only multiplications, comparisons and one f32 square root per
+            // row: S * (1/n) is within an f64 ulp of S / n, far below the f32
+            // result, and the bound needs no more than an upper estimate.
             const double dn = (double)n;
-            double mean = S / dn;
+            double mean = S * inv_n;
             const double Sd = S - dn * (double)anc;
-            double var = (Q - Sd * Sd / dn) / dn;
-            const double u = 5.9604644775390625e-08;  // 2^-24
+            double var = (Q - Sd * Sd * inv_n) * inv_n;
+            constexpr double kL = NV >= 8 ? 5.0 : NV >= 4 ? 4.0 : NV >= 2 ? 3.0 : 2.0;  // 2 + log2(NV)
+            constexpr double kLu = kL * 5.9604644775390625e-08;                           // L * 2^-24
             const double big = 1.7976931348623157e308;
             // sum |x| <= n |a| + sum |x - a| <= n |a| + sqrt(n Q) (Cauchy-Schwarz;
-            // Q's own f32 error is far below the slack this bound needs)
-            const double A = dn * fabs((double)anc) + sqrt(dn * Q);
+            // Q's own f32 error is far below the slack this bound needs).  The
+            // f32 root (correctly rounded, of an argument rounded to f32) is
+            // raised by 2^-20 to stay an upper bound; an argument past the f32
+            // range gives inf and the exact path.
+            const double A = dn * fabs((double)anc) + (double)sqrtf((float)(dn * Q)) * (1.0 + 9.5367431640625e-07);
             const bool fast = fabs(S) <= big && Q <= big && var > 1e-30 &&
-                              (2.0 + log2((double)NV)) * u * A / dn <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0) &&
+                              kLu * A * inv_n <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0) &&
                               Q <= 4.0 * dn * var;
             if (!fast) {
                 // block-uniform fallback: exact f64 two-pass (the partials of
@@ -574,7 +596,7 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 e = 0.0;
 #pragma unroll
                 for (int w = 0; w < TB / 32; ++w) e += s_d[0][par][w];
-                mean = e / dn;
+                mean = e * inv_n;
                 double q = 0.0;
 #pragma unroll
                 for (int j = 0; j < NV; ++j) {
@@ -589,7 +611,7 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 q = 0.0;
 #pragma unroll
                 for (int w = 0; w < TB / 32; ++w) q += s_d[1][par][w];
-                var = q / dn;
+                var = q * inv_n;
             }
             const float m32 = (float)mean;
             const double delta = mean - (double)m32;
@@ -797,27 +819,40 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
         return check_launch();
     };
     const bool cap = op == ROW_ARGMAX || op == STREAM_STATS + STATS_MOMENTS;
-    if (tb == 128 && cap) {
+    const int fam = op == ROW_SUM || op == ROW_MEAN                             ? FAM_SUM
+                    : op == ROW_MIN || op == ROW_MAX || op == ROW_ARGMAX        ? FAM_EXTREME
+                    : op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
+                              op == STREAM_STATS + STATS_LOGSUMEXP
+                        ? FAM_EXP
+                        : FAM_MOMENTS;
+    auto with_nv = [&](auto tb_c, auto cap_c, auto fam_c) -> int {
+        constexpr int TBc = decltype(tb_c)::value;
+        constexpr bool CAPc = decltype(cap_c)::value;
+        constexpr int F = decltype(fam_c)::value;
         switch (nv) {
-            case 1: return launch(rows_stream_kernel<T, 1, 128, true>, 128);
-            case 2: return launch(rows_stream_kernel<T, 2, 128, true>, 128);
-            case 4: return launch(rows_stream_kernel<T, 4, 128, true>, 128);
-            default: return launch(rows_stream_kernel<T, 8, 128, true>, 128);
+            case 1: return launch(rows_stream_kernel<T, 1, TBc, CAPc, F>, TBc);
+            case 2: return launch(rows_stream_kernel<T, 2, TBc, CAPc, F>, TBc);
+            case 4: return launch(rows_stream_kernel<T, 4, TBc, CAPc, F>, TBc);
+            default: return launch(rows_stream_kernel<T, 8, TBc, CAPc, F>, TBc);
         }
-    }
-    if (tb == 128) {
-        switch (nv) {
-            case 1: return launch(rows_stream_kernel<T, 1, 128, false>, 128);
-            case 2: return launch(rows_stream_kernel<T, 2, 128, false>, 128);
-            case 4: return launch(rows_stream_kernel<T, 4, 128, false>, 128);
-            default: return launch(rows_stream_kernel<T, 8, 128, false>, 128);
+    };
+    using I128 = std::integral_constant<int, 128>;
+    using I256 = std::integral_constant<int, 256>;
+    using Cap = std::true_type;
+    using NoCap = std::false_type;
+    auto with_fam = [&](auto fam_c) -> int {
+        constexpr int F = decltype(fam_c)::value;
+        if (tb == 128 && cap) {
+            if constexpr (F == FAM_EXTREME || F == FAM_MOMENTS) return with_nv(I128{}, Cap{}, fam_c);
         }
-    }
-    switch (nv) {
-        case 1: return launch(rows_stream_kernel<T, 1, 256, false>, 256);
-        case 2: return launch(rows_stream_kernel<T, 2, 256, false>, 256);
-        case 4: return launch(rows_stream_kernel<T, 4, 256, false>, 256);
-        default: return launch(rows_stream_kernel<T, 8, 256, false>, 256);
+        if (tb == 128) return with_nv(I128{}, NoCap{}, fam_c);
+        return with_nv(I256{}, NoCap{}, fam_c);
+    };
+    switch (fam) {
+        case FAM_SUM: return with_fam(std::integral_constant<int, FAM_SUM>{});
+        case FAM_EXTREME: return with_fam(std::integral_constant<int, FAM_EXTREME>{});
+        case FAM_EXP: return with_fam(std::integral_constant<int, FAM_EXP>{});
+        default: return with_fam(std::integral_constant<int, FAM_MOMENTS>{});
     }
 }
 
