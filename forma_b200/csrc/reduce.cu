@@ -468,19 +468,22 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
             m = s_f[par][0];
 #pragma unroll
             for (int w = 1; w < TB / 32; ++w) m = fmaxf(m, s_f[par][w]);
-            constexpr float kLog2e = 1.4426950408889634f;
-            float e = 0.0f;
+            // lane pairs: two values per add / multiply instruction
+            const float2 nm2 = make_float2(-m, -m);
+            const float2 l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
+            float2 e2 = make_float2(0.0f, 0.0f);
             const bool keep = op == STREAM_STATS + STATS_SOFTMAX;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 if (!valid(j)) continue;
-                const float4 x = c[j];
-                const float4 ex = make_float4(ex2_approx((x.x - m) * kLog2e), ex2_approx((x.y - m) * kLog2e),
-                                              ex2_approx((x.z - m) * kLog2e), ex2_approx((x.w - m) * kLog2e));
-                e += (ex.x + ex.y) + (ex.z + ex.w);
-                if (keep) c[j] = ex;
+                const float2 t01 = __fmul2_rn(__fadd2_rn(make_float2(c[j].x, c[j].y), nm2), l2e);
+                const float2 t23 = __fmul2_rn(__fadd2_rn(make_float2(c[j].z, c[j].w), nm2), l2e);
+                const float2 x01 = make_float2(ex2_approx(t01.x), ex2_approx(t01.y));
+                const float2 x23 = make_float2(ex2_approx(t23.x), ex2_approx(t23.y));
+                e2 = __fadd2_rn(e2, __fadd2_rn(x01, x23));
+                if (keep) c[j] = make_float4(x01.x, x01.y, x23.x, x23.y);
             }
-            e = warp_sum_f(e);
+            float e = warp_sum_f(e2.x + e2.y);
             if (lane == 0) s_e[par][warp] = e;
             __syncthreads();
             e = 0.0f;
@@ -488,64 +491,72 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
             for (int w = 0; w < TB / 32; ++w) e += s_e[par][w];
             if (op == STREAM_STATS + STATS_SOFTMAX) {
                 const float inv = __frcp_rn(e);
+                const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
-                    if (valid(j))
-                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
-                                   make_float4(c[j].x * inv, c[j].y * inv, c[j].z * inv, c[j].w * inv));
+                    if (valid(j)) {
+                        const float2 y01 = __fmul2_rn(make_float2(c[j].x, c[j].y), inv2);
+                        const float2 y23 = __fmul2_rn(make_float2(c[j].z, c[j].w), inv2);
+                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4, make_float4(y01.x, y01.y, y23.x, y23.y));
+                    }
             } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
                 // (x - max) - log(sum): both terms within an f32 ulp
                 const float ls = logf(e);
+                const float2 nls = make_float2(-ls, -ls);
 #pragma unroll
                 for (int j = 0; j < NV; ++j)
-                    if (valid(j))
-                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4,
-                                   make_float4((c[j].x - m) - ls, (c[j].y - m) - ls, (c[j].z - m) - ls,
-                                               (c[j].w - m) - ls));
+                    if (valid(j)) {
+                        const float2 y01 = __fadd2_rn(__fadd2_rn(make_float2(c[j].x, c[j].y), nm2), nls);
+                        const float2 y23 = __fadd2_rn(__fadd2_rn(make_float2(c[j].z, c[j].w), nm2), nls);
+                        store_row4(eo, row, (tid + (uint64_t)j * TB) * 4, make_float4(y01.x, y01.y, y23.x, y23.y));
+                    }
             } else if (tid == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log((double)e));
             }
         } else {  // FAM_MOMENTS
             // Moments / layer norm in one pass and one block reduction.  Each
-            // thread sums, per float4, x (pairwise f32, f64 across float4s) and
-            // (x - a)^2 around an anchor
-            // a = the mean of the row's first four values (read from the staged
-            // row, identical in every thread).  Then
-            //   mean = S / n,   var = (Q - (S - n a)^2 / n) / n.
+            // thread sums the deviations d = x - a from an anchor a (the mean
+            // of the row's first four values, read from the staged row,
+            // identical in every thread) and their squares, in f32 lane pairs
+            // (two values per instruction) combined pairwise, then in f64
+            // across lanes, warps and the block:
+            //   D = sum d,  Q = sum d^2,  mean = a + D / n,  var = (Q - D^2 / n) / n.
             // Accepted when both error bounds leave a wide margin under the
-            // 1e-5 tolerance (u = 2^-24):
-            //   mean:  L u * A / n <= 2^-20 * max(|mean|, 1)   (A bounds sum |x|
-            //          as n |a| + sqrt(n Q), L = 2 + log2(NV): the depth of
-            //          the f32 pairwise tree)
+            // 1e-5 tolerance (u = 2^-24; the f32 tree has depth L = 2 + log2(NV)
+            // after the rounding of each d):
+            //   mean:  (L + 1) u * sum |d| / n <= 2^-20 * max(|mean|, 1), with
+            //          sum |d| <= sqrt(n Q) (Cauchy-Schwarz)
             //   var:   Q <= 4 * n * var  (cancellation factor <= 4; each f32
             //          partial of squares is within (L + 3) u, so var is
-            //          within 4 (L + 3) u, <= 28u)
+            //          within 4 (L + 3) u, <= 32u)
             // and everything is finite with a variance that cannot have
-            // underflowed in f32; otherwise (NaN/inf inputs, huge offsets
-            // from the anchor, constant rows) the row is redone exactly in f64
-            // with two passes, as the reference computes it (statistics.cu:4-123).
+            // underflowed in f32; otherwise (NaN/inf inputs, constant rows,
+            // deviations too large for the bounds) the row is redone exactly
+            // in f64 with two passes, as the reference computes it
+            // (statistics.cu:4-123).
             const float4 head = smem_load4<T>(rb, 0);
             const float anc = 0.25f * ((head.x + head.y) + (head.z + head.w));
-            // per-float4 f32 partials, combined pairwise in f32 (depth log2(4 NV))
-            float s4[NV], q4[NV];
+            const float2 na2 = make_float2(-anc, -anc);
+            float2 s2[NV], q2[NV];
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 if (!valid(j)) {
-                    s4[j] = q4[j] = 0.0f;
+                    s2[j] = q2[j] = make_float2(0.0f, 0.0f);
                     continue;
                 }
-                const float d0 = c[j].x - anc, d1 = c[j].y - anc, d2 = c[j].z - anc, d3 = c[j].w - anc;
-                s4[j] = (c[j].x + c[j].y) + (c[j].z + c[j].w);
-                q4[j] = fmaf(d0, d0, d1 * d1) + fmaf(d2, d2, d3 * d3);
+                const float2 d01 = __fadd2_rn(make_float2(c[j].x, c[j].y), na2);
+                const float2 d23 = __fadd2_rn(make_float2(c[j].z, c[j].w), na2);
+                s2[j] = __fadd2_rn(d01, d23);
+                q2[j] = __ffma2_rn(d01, d01, __fmul2_rn(d23, d23));
             }
 #pragma unroll
             for (int w = 1; w < NV; w *= 2)
 #pragma unroll
                 for (int j = 0; j + w < NV; j += 2 * w) {
-                    s4[j] += s4[j + w];
-                    q4[j] += q4[j + w];
+                    s2[j] = __fadd2_rn(s2[j], s2[j + w]);
+                    q2[j] = __fadd2_rn(q2[j], q2[j + w]);
                 }
-            double sd = (double)s4[0], qd = (double)q4[0];
+            double sd = (double)s2[0].x + (double)s2[0].y, qd = (double)q2[0].x + (double)q2[0].y;
             sd = warp_sum(sd);
             qd = warp_sum(qd);
             if (lane == 0) {
@@ -557,29 +568,26 @@ __global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, u
                 aborted_at = i;
                 break;
             }
-            double S = 0.0, Q = 0.0;
+            double D = 0.0, Q = 0.0;
 #pragma unroll
             for (int w = 0; w < TB / 32; ++w) {
-                S += s_d[0][par][w];
+                D += s_d[0][par][w];
                 Q += s_d[1][par][w];
             }
             // Only multiplications, comparisons and one f32 square root per
-            // row: S * (1/n) is within an f64 ulp of S / n, far below the f32
+            // row: D * (1/n) is within an f64 ulp of D / n, far below the f32
             // result, and the bound needs no more than an upper estimate.
             const double dn = (double)n;
-            double mean = S * inv_n;
-            const double Sd = S - dn * (double)anc;
-            double var = (Q - Sd * Sd * inv_n) * inv_n;
-            constexpr double kL = NV >= 8 ? 5.0 : NV >= 4 ? 4.0 : NV >= 2 ? 3.0 : 2.0;  // 2 + log2(NV)
-            constexpr double kLu = kL * 5.9604644775390625e-08;                           // L * 2^-24
+            double mean = (double)anc + D * inv_n;
+            double var = (Q - D * D * inv_n) * inv_n;
+            constexpr double kL = NV >= 8 ? 6.0 : NV >= 4 ? 5.0 : NV >= 2 ? 4.0 : 3.0;  // 3 + log2(NV)
+            constexpr double kLu = kL * 5.9604644775390625e-08;                           // (L + 1) * 2^-24
             const double big = 1.7976931348623157e308;
-            // sum |x| <= n |a| + sum |x - a| <= n |a| + sqrt(n Q) (Cauchy-Schwarz;
-            // Q's own f32 error is far below the slack this bound needs).  The
-            // f32 root (correctly rounded, of an argument rounded to f32) is
-            // raised by 2^-20 to stay an upper bound; an argument past the f32
-            // range gives inf and the exact path.
-            const double A = dn * fabs((double)anc) + (double)sqrtf((float)(dn * Q)) * (1.0 + 9.5367431640625e-07);
-            const bool fast = fabs(S) <= big && Q <= big && var > 1e-30 &&
+            // The f32 root (correctly rounded, of an argument rounded to f32)
+            // is raised by 2^-20 to stay an upper bound; an argument past the
+            // f32 range gives inf and the exact path.
+            const double A = (double)sqrtf((float)(dn * Q)) * (1.0 + 9.5367431640625e-07);
+            const bool fast = fabs(D) <= big && Q <= big && var > 1e-30 &&
                               kLu * A * inv_n <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0) &&
                               Q <= 4.0 * dn * var;
             if (!fast) {
