@@ -698,6 +698,93 @@ __global__ void __launch_bounds__(BLOCK) sum_partial_kernel(Rows in, double* blo
     }
 }
 
+// Global f32 sum, streamed: the input is cut into 16 KB chunks dealt to the
+// blocks round-robin (chunk b, b + grid, ...); each block streams its chunks
+// HBM -> shared memory through a cp.async.bulk ring and every thread adds its
+// float4s into one f64 across all its chunks (no per-chunk reduction, one
+// barrier per chunk to release the ring slot).  The elements after the last
+// full chunk are added by the last block with plain loads; the block partials
+// are then folded in index order by the last block to finish.  The chunk
+// assignment is fixed by the grid, so the result does not depend on block
+// scheduling.
+constexpr uint32_t kSumChunk = 4096;  // floats per chunk
+constexpr int kSumTB = 128;
+constexpr int kSumNV = kSumChunk / 4 / kSumTB;  // float4s per thread per chunk
+
+__global__ void __launch_bounds__(kSumTB) sum_stream_kernel(const float* base, uint64_t chunks, uint64_t tail_n,
+                                                           uint32_t stages, double* block_partials, unsigned* counter,
+                                                           double* result) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    unsigned char* ring = smem + 128;
+    __shared__ double s_sum[kSumTB / 32];
+    __shared__ bool s_last;
+    __shared__ int s_abort;
+    constexpr uint32_t kBytes = kSumChunk * 4;
+    const uint32_t tid = threadIdx.x;
+    const uint64_t first = blockIdx.x, step = gridDim.x;
+    const uint64_t mine = first < chunks ? (chunks - 1 - first) / step + 1 : 0;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    auto issue = [&](uint64_t i) {
+        const uint32_t s = (uint32_t)(i % stages);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[s], kBytes);
+        bulk_g2s(ring + (uint64_t)s * kBytes, base + (first + i * step) * kSumChunk, kBytes, &full[s]);
+    };
+    if (tid == 0)
+        for (uint64_t i = 0; i < mine && i < stages; ++i) issue(i);
+    double acc = 0.0;
+    uint64_t aborted_at = ~0ull;
+    for (uint64_t i = 0; i < mine; ++i) {
+        const uint32_t s = (uint32_t)(i % stages);
+        if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) s_abort = 1;
+        const float4* rb = reinterpret_cast<const float4*>(ring + (uint64_t)s * kBytes);
+        float4 x[kSumNV];
+#pragma unroll
+        for (int j = 0; j < kSumNV; ++j) x[j] = rb[tid + j * kSumTB];
+        __syncthreads();  // every thread has read slot s
+        if (s_abort) {
+            aborted_at = i;
+            break;
+        }
+        if (tid == 0 && i + stages < mine) issue(i + stages);
+#pragma unroll
+        for (int j = 0; j < kSumNV; ++j)
+            acc += ((double)x[j].x + (double)x[j].y) + ((double)x[j].z + (double)x[j].w);
+    }
+    if (aborted_at != ~0ull && tid == 0) {
+        atomicOr(&g_reduce_status, 1u << DEV_ROWS_WAIT_TIMEOUT);
+        for (uint64_t i = aborted_at; i < mine && i < aborted_at + stages; ++i)
+            (void)mbar_wait(&full[i % stages], (uint32_t)((i / stages) & 1));
+    }
+    if (blockIdx.x == gridDim.x - 1)
+        for (uint64_t c = tid; c < tail_n; c += kSumTB) acc += (double)base[chunks * kSumChunk + c];
+    // The finishing protocol runs even after a timeout (the status word
+    // reports it), so that the counter is re-armed for the next call.
+    acc = block_sum<kSumTB>(acc, s_sum);
+    if (tid == 0) {
+        block_partials[blockIdx.x] = acc;
+        __threadfence();
+        s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        double t = 0.0;
+        for (unsigned b = tid; b < gridDim.x; b += kSumTB) t += __ldcg(block_partials + b);
+        t = block_sum<kSumTB>(t, s_sum);
+        if (tid == 0) {
+            *result = t;
+            *counter = 0u;
+        }
+    }
+}
+
 __global__ void finish_sum_kernel(const double* partial, float* out) { *out = (float)*partial; }
 
 __global__ void fill_kernel(uint32_t* out, uint64_t count, uint32_t bits) {
@@ -918,12 +1005,35 @@ int launch_stats_rows(uint32_t op, const Rows& in, const ElemOut& out, const Row
 
 int launch_sum_partial(const Rows& in, double* partial, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Scratch layout: [u32 counter, padded to 256 bytes][block partials], the
+    // same for both kernels so that the counter every call re-arms is shared.
+    const float* base = reinterpret_cast<const float*>(in.data) + in.offset;
+    if (in.rows == 1 && in.contiguous_rows && reinterpret_cast<uintptr_t>(base) % 16 == 0 &&
+        in.cols >= (uint64_t)kSumChunk * (uint64_t)sm_count()) {
+        const uint32_t stages = 2;
+        const size_t smem = 128 + (size_t)stages * kSumChunk * 4;
+        if (cudaFuncSetAttribute(sum_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return FB_ERR_DRIVER;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sum_stream_kernel, kSumTB, smem) != cudaSuccess ||
+            per_sm < 1)
+            return FB_ERR_DRIVER;
+        const uint64_t chunks = in.cols / kSumChunk;
+        const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
+        const unsigned g = (unsigned)(chunks < cap ? chunks : cap);
+        char* scr = static_cast<char*>(scratch(stream, 256 + (uint64_t)g * sizeof(double), SCRATCH_SUM));
+        if (!scr) return FB_ERR_DRIVER;
+        sum_stream_kernel<<<g, kSumTB, smem, s>>>(base, chunks, in.cols % kSumChunk, stages,
+                                                   reinterpret_cast<double*>(scr + 256),
+                                                   reinterpret_cast<unsigned*>(scr), partial);
+        return check_launch();
+    }
     const unsigned g = (unsigned)sm_count() * 4;
-    // Scratch layout: [g doubles of block partials][one u32 counter].
-    char* scr = static_cast<char*>(scratch(stream, (uint64_t)g * sizeof(double) + 256, SCRATCH_SUM));
+    char* scr = static_cast<char*>(scratch(stream, 256 + (uint64_t)g * sizeof(double), SCRATCH_SUM));
     if (!scr) return FB_ERR_DRIVER;
-    double* partials = reinterpret_cast<double*>(scr);
-    unsigned* counter = reinterpret_cast<unsigned*>(scr + (uint64_t)g * sizeof(double));
+    double* partials = reinterpret_cast<double*>(scr + 256);
+    unsigned* counter = reinterpret_cast<unsigned*>(scr);
     if (vec_ok(in))
         sum_partial_kernel<4><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
     else

@@ -260,6 +260,15 @@ def test_global_sum(cuda):
     for _ in range(3):
         got = api.sum_partial_f64(t.t()).item()
         assert abs(got - want) <= 1e-9 * max(abs(want), 1.0)
+    # streamed chunks with a ragged tail, a 16-byte-misaligned view (plain
+    # loads), alternating so that both kernels share the re-armed counter
+    flat = _rows(1, 4096 * 300 + 123, seed=10)[0]
+    ft = torch.from_numpy(flat).to(cuda)
+    for view in (ft, ft[1:], ft, ft[3:], ft):
+        want = orc.sum_f64(view.cpu().numpy())
+        got = api.sum_partial_f64(view).item()
+        assert abs(got - want) <= 1e-9 * max(abs(want), 1.0)
+    assert api.device_status() == 0
 
 
 def test_full_size_row_workload_properties(cuda):
