@@ -1,10 +1,14 @@
 // Fused flash attention on the 5th-generation tensor cores (tcgen05).
 //
-// attention_low_f32 for 16-bit Q/K/V, depth D in {64, 128}, no mask tensor,
-// optional causal offset.  One CTA owns 256 query rows (two 128-row Q tiles)
-// of one (batch, head) and streams that head's K/V once for both tiles.
-//   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys
-//               into a 2-stage ring (128B-swizzled boxes of 64 depth columns).
+// attention_low_f32 for 16-bit Q/K/V, depth D in {64, 128}, keep / additive
+// masks, optional causal offset.  One CTA owns 256 query rows (two 128-row Q
+// tiles) of one (batch, head) and streams that head's K/V once for both tiles.
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128
+//               keys into rings of 2 (D = 128) or 4 (D = 64) slots with their
+//               own full/empty barriers (128B-swizzled boxes of 64 depth
+//               columns).  A K slot is released as soon as both tiles' S of
+//               that key tile are computed, a key step before its V, so K
+//               tiles load two key steps ahead of their use.
 //   warp 1      TMEM allocator and MMA issuer (the whole warp runs the issue
 //               loop; one elected lane issues).  Per key tile j, per Q tile t:
 //                 S_t = Q_t K_j^T  -> TMEM S_t (128 x 128 f32)
@@ -180,9 +184,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
     unsigned char* sKV = sQ + QT * C::Q_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::STAGES * C::STAGE_BYTES);
     uint64_t* q_full = bars;                           // 1
-    uint64_t* kv_full = bars + 1;                      // STAGES
-    uint64_t* kv_empty = kv_full + C::STAGES;          // STAGES
-    uint64_t* s_full = kv_empty + C::STAGES;           // QT
+    uint64_t* k_full = bars + 1;                       // STAGES
+    uint64_t* k_empty = k_full + C::STAGES;            // STAGES
+    uint64_t* v_full = k_empty + C::STAGES;            // STAGES
+    uint64_t* v_empty = v_full + C::STAGES;            // STAGES
+    uint64_t* s_full = v_empty + C::STAGES;            // QT
     uint64_t* p_full = s_full + QT;                    // QT
     uint64_t* o_done = p_full + QT;                    // QT
     uint64_t* drain = o_done + QT;                     // 1
@@ -210,8 +216,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         for (int t = 0; t < QT; ++t) {
             mbar_init(&s_full[t], 1);
@@ -239,27 +247,39 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
                     tma_load_4d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, (int32_t)(q0 + t * TQ), (int32_t)head,
                                 (int32_t)batch, q_full);
         }
-        uint32_t issued = 0;
+        // K and V have their own slots and barriers: K(j) is released once
+        // both tiles' S(j) are computed, a key step before V(j), so the
+        // next K tiles load two key steps ahead of their use.
+        uint32_t issued_k = 0, issued_v = 0;
         bool failed = false;
         for (uint32_t j = 0; j < n_kv; ++j) {
-            const uint32_t s = j % C::STAGES;
-            if (!mbar_wait(&kv_empty[s], ((j / C::STAGES) & 1) ^ 1)) {
+            const uint32_t s = j % C::STAGES, ph = ((j / C::STAGES) & 1) ^ 1;
+            unsigned char* kd = sKV + s * C::STAGE_BYTES;
+            unsigned char* vd = kd + C::K_BYTES;
+            if (!mbar_wait(&k_empty[s], ph)) {
                 failed = true;
                 break;
             }
-            unsigned char* kd = sKV + s * C::STAGE_BYTES;
-            unsigned char* vd = kd + C::K_BYTES;
-            mbar_arrive_expect_tx(&kv_full[s], C::STAGE_BYTES);
-            for (int b = 0; b < C::BOXES; ++b) {
-                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)(j * TK), kv_head, k_b, &kv_full[s]);
-                tma_load_4d(vd + b * (TK * 128), &tmV, b * 64, (int32_t)(j * TK), kv_head, v_b, &kv_full[s]);
+            mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
+            for (int b = 0; b < C::BOXES; ++b)
+                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)(j * TK), kv_head, k_b, &k_full[s]);
+            ++issued_k;
+            if (!mbar_wait(&v_empty[s], ph)) {
+                failed = true;
+                break;
             }
-            ++issued;
+            mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+            for (int b = 0; b < C::BOXES; ++b)
+                tma_load_4d(vd + b * (TK * 128), &tmV, b * 64, (int32_t)(j * TK), kv_head, v_b, &v_full[s]);
+            ++issued_v;
         }
         if (failed) {
+            // drain the copies still in flight (bounded) before exiting
             atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
-            for (uint32_t j = issued >= C::STAGES ? issued - C::STAGES : 0; j < issued; ++j)
-                (void)mbar_wait(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+            for (uint32_t j = issued_k >= C::STAGES ? issued_k - C::STAGES : 0; j < issued_k; ++j)
+                (void)mbar_wait(&k_full[j % C::STAGES], (j / C::STAGES) & 1);
+            for (uint32_t j = issued_v >= C::STAGES ? issued_v - C::STAGES : 0; j < issued_v; ++j)
+                (void)mbar_wait(&v_full[j % C::STAGES], (j / C::STAGES) & 1);
         }
         if (n_kv > 0) (void)mbar_wait(q_full, 0);
     } else if (warp == 1) {
@@ -273,7 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         bool ok = n_kv == 0 || wait(q_full, 0);
         auto issue_s = [&](int t, uint32_t j) -> bool {
             const uint32_t s = j % C::STAGES;
-            if (!wait(&kv_full[s], (j / C::STAGES) & 1)) return false;
+            if (!wait(&k_full[s], (j / C::STAGES) & 1)) return false;
             tc_fence_after();
             const uint64_t qd = sw128_desc(smem_u32(sQ + t * C::Q_BYTES));
             const uint64_t kd = sw128_desc(smem_u32(sKV + s * C::STAGE_BYTES));
@@ -288,6 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         };
         auto issue_pv = [&](int t, uint32_t j) -> bool {
             const uint32_t s = j % C::STAGES;
+            if (!wait(&v_full[s], (j / C::STAGES) & 1)) return false;
             if (!wait(&p_full[t], j & 1)) return false;
             tc_fence_after();
             const uint64_t vd = sw128_mn_desc(smem_u32(sKV + s * C::STAGE_BYTES + C::K_BYTES), TK * 128);
@@ -300,14 +321,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_const
         };
         for (int t = 0; t < QT && ok; ++t)
             if (n_t[t] > 0) ok = issue_s(t, 0);
+        if (ok && n_kv > 0) umma_commit_warp(&k_empty[0]);  // K(0) consumed by every S(0)
         for (uint32_t j = 0; ok && j < n_kv; ++j) {
             for (int t = 0; t < QT && ok; ++t) {
                 if (j >= n_t[t]) continue;
                 ok = issue_pv(t, j);
                 if (ok && j + 1 < n_t[t]) ok = issue_s(t, j + 1);
             }
-            // stage j is free once every PV reading it has completed
-            if (ok) umma_commit_warp(&kv_empty[j % C::STAGES]);
+            // V(j) is free once every PV(j) has completed, K(j + 1) once
+            // every S(j + 1) has
+            if (ok) umma_commit_warp(&v_empty[j % C::STAGES]);
+            if (ok && j + 1 < n_kv) umma_commit_warp(&k_empty[(j + 1) % C::STAGES]);
         }
         if (!ok && lane == 0) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
         umma_commit_warp(drain);
