@@ -86,7 +86,7 @@ def test_tc_conv_c3_shapes_sampled(cuda):
         opts = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
         out = api.conv_low_f32(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2), opts)
         assert api.device_status() == 0
-        for img in (0, 131, 255):
+        for img in (0, 37, 131, 200, 255):
             ref = orc.conv(x[img:img + 1].permute(0, 3, 1, 2).float().cpu().numpy(),
                            w.permute(0, 3, 1, 2).float().cpu().numpy(), [1, 1], [1, 1], [pad] * 2, [pad] * 2, 1,
                            nthreads=orc.threads())

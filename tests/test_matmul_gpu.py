@@ -77,3 +77,27 @@ def test_matmul_empty_contraction_and_errors(cuda):
     with pytest.raises(api.TensorError) as e:
         api.matmul_low_f32(rnd(3, 4).to(cuda), rnd(4, 2, dtype=torch.float16).to(cuda))
     assert e.value.kind == "InvalidInput"
+
+
+@pytest.mark.parametrize("M,K,N", [(19200, 512, 256), (19200, 2048, 512), (12608, 768, 768)])
+def test_matmul_many_tiles(cuda, M, K, N):
+    """More output tiles than persistent CTAs (several per CTA, a partial
+    last wave, both TMEM accumulators in turn): results against an f32
+    product on the GPU with TF32 off, bit-identical across repeated calls."""
+    g = torch.Generator(device=cuda).manual_seed(M + K + N)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    b = torch.randn(K, N, device=cuda, generator=g).bfloat16()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = a.float() @ b.float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    first = api.matmul_low_f32(a, b)
+    assert api.device_status() == 0
+    err = float((first - ref).abs().max()) / float(ref.abs().max())
+    assert err <= 1e-4, err
+    for _ in range(2):
+        again = api.matmul_low_f32(a, b)
+        assert torch.equal(again, first)
+    assert api.device_status() == 0
