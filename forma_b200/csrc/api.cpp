@@ -475,8 +475,11 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     a.scale = plan.scale;
     a.causal = plan.causal;
     a.causal_offset = plan.causal_offset;
-    int s = FB_ERR_UNSUPPORTED;
-    if (low) s = launch_attention_tc(a, stream);
+    // 16-bit operands: tensor cores when the layout allows (fastest for
+    // decode shapes too); otherwise few query rows over long key ranges
+    // split the keys across warps; everything else one warp per row.
+    int s = low ? launch_attention_tc(a, stream) : FB_ERR_UNSUPPORTED;
+    if (s == FB_ERR_UNSUPPORTED) s = launch_attention_decode(a, stream);
     if (s == FB_ERR_UNSUPPORTED) s = launch_attention_simt(a, stream);
     return launched(s, "attention");
 }

@@ -80,7 +80,8 @@ enum ScratchSlot : int {
     SCRATCH_CONV_WEIGHT = 2,  // weights gathered into [O, kh, kw, C] or [O, C, kh, kw]
     SCRATCH_CONV_PATCH = 3,   // non-overlapping patches gathered into [N*P*Q, C*kh*kw]
     SCRATCH_STATS = 4,        // f32 statistics result before low rounding
-    SCRATCH_SLOTS = 5,
+    SCRATCH_ATTN_SPLIT = 5,   // split-key attention partials (f64 per row and key range)
+    SCRATCH_SLOTS = 6,
 };
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
@@ -196,6 +197,9 @@ struct AttnArgs {
     int32_t causal_offset = 0;
 };
 int launch_attention_simt(const AttnArgs& a, void* stream);
+// Split-key attention for at most 64 query rows per head over >= 512 keys;
+// FB_ERR_UNSUPPORTED for other shapes.
+int launch_attention_decode(const AttnArgs& a, void* stream);
 int launch_attention_tc(const AttnArgs& a, void* stream);
 
 }  // namespace fb
