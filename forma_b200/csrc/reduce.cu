@@ -302,11 +302,11 @@ constexpr int FAM_EXTREME = 1;  // min, max, argmax
 constexpr int FAM_EXP = 2;      // softmax, log-softmax, logsumexp
 constexpr int FAM_MOMENTS = 3;  // moments, layer norm
 
-// CAP: registers capped so that six 128-thread blocks fit per SM (argmax and
-// moments hold more per-row state and measured faster with the extra blocks;
-// the light reductions measured faster uncapped).
+// CAP: registers capped so that six (argmax) or five (moments: six spilled
+// in its row loop) 128-thread blocks fit per SM; both hold more per-row state
+// and measured faster with the extra blocks, the light reductions uncapped.
 template <typename T, int NV, int TB, bool CAP, int FAM>
-__global__ void __launch_bounds__(TB, CAP ? 6 : 1) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
+__global__ void __launch_bounds__(TB, CAP ? (FAM == FAM_MOMENTS ? 5 : 6) : 1) rows_stream_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
                                                             float eps, uint32_t stages, uint32_t row_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
