@@ -313,6 +313,267 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
     }
 }
 
+// The same GEMM on CTA pairs (2-CTA clusters, tcgen05 cta_group::2): a pair
+// owns a 256 x 256 output tile; each CTA loads its 128 rows of A and its 128
+// of the 256 B rows (half the weight traffic of two independent CTAs, 32 KB
+// per stage so six stages fit), and holds its 128 accumulator rows in its own
+// TMEM.  The even CTA's MMA warp issues every MMA (M = 256) once both CTAs'
+// loads of a stage have landed on the even CTA's `full` barrier, and its
+// commits arrive on both CTAs' `empty` / `tfull` barriers; both epilogues
+// arrive on the even CTA's `tempty`.
+struct PairCfg {
+    static constexpr int BN = 256;                 // pair tile N; each CTA loads BN / 2 rows of B
+    static constexpr int A_BYTES = BM * BK * 2;    // 16 KB
+    static constexpr int B_BYTES = BN / 2 * BK * 2;  // 16 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = 6;
+    static constexpr int TMEM_COLS = 512;          // two 256-column accumulators
+    static constexpr int EPI_PITCH = 36;
+    static constexpr int EPI_BYTES = 4 * 32 * EPI_PITCH * 4;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    conv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          ConvGemmParams p) {
+    using C = PairCfg;
+    constexpr int BN = C::BN;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* ring = smem;
+    float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
+    uint64_t* full = bars;                     // [STAGES] used in the even CTA
+    uint64_t* empty = bars + C::STAGES;        // [STAGES]
+    uint64_t* tfull = bars + 2 * C::STAGES;    // [2]
+    uint64_t* tempty = tfull + 2;              // [2] used in the even CTA
+    uint64_t* drain = tempty + 2;              // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const uint32_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const uint32_t m_pairs = (p.m_tiles + 1) / 2;
+    const uint32_t tiles = m_pairs * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * 4 * 32);  // both CTAs' epilogue threads
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool failed = false;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        const uint32_t full0 = mapa_u32(smem_u32(full), 0);
+        uint32_t stage = 0, phase = 0;
+        uint64_t issued = 0;
+        for (uint32_t t = pair; t < tiles && !failed; t += pairs) {
+            const uint32_t mt = t / p.n_tiles, nt = t % p.n_tiles;
+            const uint32_t m0 = mt * 2 * BM + rank * BM;
+            const uint32_t pq = p.P * p.Q;
+            const int32_t n0 = (int32_t)(m0 / pq), rem = (int32_t)(m0 % pq);
+            const int32_t w0 = (rem % (int32_t)p.Q) * p.stride_w - p.pad_w;
+            const int32_t h0 = (rem / (int32_t)p.Q) * p.stride_h - p.pad_h;
+            const int32_t b0 = (int32_t)(nt * BN + rank * (BN / 2));
+            for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1)) {
+                    atomicOr(&g_gemm_status, 1u << DEV_GEMM_PRODUCER_TIMEOUT);
+                    failed = true;
+                    break;
+                }
+                unsigned char* a_dst = ring + stage * C::STAGE_BYTES;
+                unsigned char* b_dst = a_dst + C::A_BYTES;
+                const uint32_t bar = full0 + (uint32_t)(stage * sizeof(uint64_t));
+                if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both CTAs' bytes
+                const uint32_t cb = kb % p.c_blocks, tap = kb / p.c_blocks;
+                if (p.mode == 0) {
+                    tma_load_2d_pair(a_dst, &tmA, (int32_t)(cb * BK), (int32_t)m0, bar);
+                } else {
+                    const uint32_t r = tap / p.S, s = tap % p.S;
+                    tma_load_im2col_4d_pair(a_dst, &tmA, (int32_t)(cb * BK), w0, h0, n0, (uint16_t)(s * p.dil_w),
+                                            (uint16_t)(r * p.dil_h), bar);
+                }
+                if (p.b_mn) {
+#pragma unroll
+                    for (int nb = 0; nb < BN / 2 / 64; ++nb)
+                        tma_load_2d_pair(b_dst + nb * (BK * 128), &tmB, b0 + nb * 64, (int32_t)(kb * BK), bar);
+                } else {
+                    tma_load_2d_pair(b_dst, &tmB, (int32_t)(kb * BK), b0, bar);
+                }
+                ++issued;
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        if (failed) {
+            // Loads already issued land on the even CTA's barrier; give them
+            // time to complete before the CTA can exit (bounded).
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 200000ull) {
+            }
+        }
+    } else if (warp == 1 && leader) {
+        // ------------------------------------------------ MMA issuer (even CTA)
+        const uint32_t idesc = f16_idesc(p.fmt, 2 * BM, BN);
+        const uint32_t idesc_mn = idesc | (1u << 16);
+        auto wait = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
+        uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+        for (uint32_t t = pair; t < tiles && !failed; t += pairs) {
+            if (!wait(&tempty[acc], acc_phase ^ 1)) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + acc * BN;
+            for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                if (!wait(&full[stage], phase)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t ad = sw128_desc(smem_u32(ring + stage * C::STAGE_BYTES));
+                if (p.b_mn) {
+                    const uint64_t bd = sw128_mn_desc(smem_u32(ring + stage * C::STAGE_BYTES + C::A_BYTES), BK * 128);
+                    umma_f16_ss_pair_warp(d, ad, bd, idesc_mn, kb != 0);
+#pragma unroll
+                    for (int k = 1; k < BK / 16; ++k)
+                        umma_f16_ss_pair_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 16 * 128), idesc_mn, 1u);
+                } else {
+                    const uint64_t bd = desc_add(ad, C::A_BYTES);
+                    umma_f16_ss_pair_warp(d, ad, bd, idesc, kb != 0);
+#pragma unroll
+                    for (int k = 1; k < BK / 16; ++k)
+                        umma_f16_ss_pair_warp(d, desc_add(ad, k * 32), desc_add(bd, k * 32), idesc, 1u);
+                }
+                umma_commit_pair_warp(&empty[stage], 0x3);  // frees the stage in both CTAs
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (failed) break;
+            umma_commit_pair_warp(&tfull[acc], 0x3);  // accumulator rows complete in both CTAs
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (failed && lane == 0) atomicOr(&g_gemm_status, 1u << DEV_GEMM_MMA_TIMEOUT);
+        umma_commit_pair_warp(drain, 0x1);
+        (void)wait(drain, 0);
+    } else if (warp >= 2) {
+        // ------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t tempty0 = mapa_u32(smem_u32(tempty), 0);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t t = pair; t < tiles; t += pairs) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase))) {
+                atomicOr(&g_gemm_status, 1u << DEV_GEMM_EPILOGUE_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t mt = t / p.n_tiles, nt = t % p.n_tiles;
+            const uint32_t m = mt * 2 * BM + rank * BM + row;
+            uint64_t base = ~0ull;
+            if (m < p.M) {
+                const uint32_t pq = p.P * p.Q;
+                const uint32_t n = m / pq, r = m % pq;
+                base = p.out_offset + (uint64_t)n * p.s_n + (uint64_t)(r / p.Q) * p.s_p + (uint64_t)(r % p.Q) * p.s_q +
+                       (uint64_t)(nt * BN) * p.s_c;
+            }
+            uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
+            const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
+            if (p.c_rows) {
+                float* st = epi + quarter * (32 * C::EPI_PITCH);
+                const uint64_t my_base = base;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4*>(st + lane * C::EPI_PITCH + 4 * q) =
+                            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                        __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + (lane >> 3), cc = lane & 7;
+                        const uint64_t rb = __shfl_sync(0xffffffffu, my_base, r);
+                        const float4 val = *reinterpret_cast<const float4*>(st + r * C::EPI_PITCH + 4 * cc);
+                        if (rb != ~0ull) {
+                            if (p.out_low)
+                                *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
+                                    make_uint2(encode_low_pair(val.x, val.y, p.out_low),
+                                               encode_low_pair(val.z, val.w, p.out_low));
+                            else
+                                *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
+                        }
+                    }
+                    __syncwarp();
+                }
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
+                    if (base != ~0ull) {
+                        if (p.out_low == FB_BF16) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_bf16(__uint_as_float(v[j]));
+                        } else if (p.out_low) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_f16(__uint_as_float(v[j]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(tempty0 + (uint32_t)(acc * sizeof(uint64_t)));  // the even CTA's accumulator slot
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    // Both CTAs stay until every pair MMA has completed (the even CTA's MMA
+    // warp waited on `drain`) and every remote arrive has landed.
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------ host
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
@@ -437,6 +698,54 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams
     return launch_status("kernel launch");
 }
 
+// CTA-pair launch for N a multiple of 256 and at least two 128-row M tiles;
+// `tb_half` boxes 128 rows of K-major B (MN-major B: the usual 64 x BK box).
+// FB_ERR_UNSUPPORTED when no 2-CTA cluster can be resident.
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, const ConvGemmParams& p, cudaStream_t st) {
+    if (p.m_tiles < 2) return FB_ERR_UNSUPPORTED;
+    if (cudaFuncSetAttribute(conv_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM) !=
+        cudaSuccess)
+        return launch_status("shared-memory attribute");
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (max_clusters[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)sm_count());
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, conv_gemm_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+            (void)cudaGetLastError();
+            max_clusters[dev] = -1;
+        } else {
+            max_clusters[dev] = n;
+        }
+    }
+    if (max_clusters[dev] < 1) return FB_ERR_UNSUPPORTED;
+    const uint32_t tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
+    const uint32_t clusters = tiles < (uint32_t)max_clusters[dev] ? tiles : (uint32_t)max_clusters[dev];
+    conv_gemm_pair_kernel<<<2 * clusters, THREADS, PairCfg::SMEM, st>>>(ta, tb_half, p);
+    count_launch();
+    return launch_status("kernel launch");
+}
+
+// Dispatch by tile width: CTA pairs for BN = 256 when a half-width B map is
+// given, else one CTA per tile.
+int launch_tiles(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tb_half,
+                 const ConvGemmParams& p, cudaStream_t st) {
+    if (BN == 256 && tb_half) {
+        const int r = launch_pair(ta, *tb_half, p, st);
+        if (r != FB_ERR_UNSUPPORTED) return r;
+    }
+    switch (BN) {
+        case 256: return launch_bn<256>(ta, tb, p, st);
+        case 128: return launch_bn<128>(ta, tb, p, st);
+        default: return launch_bn<64>(ta, tb, p, st);
+    }
+}
+
 }  // namespace
 
 uint32_t read_gemm_status() {
@@ -488,10 +797,11 @@ int launch_gemm_tc(const GemmArgs& g, void* stream) {
         const uint16_t* b = static_cast<const uint16_t*>(g.b) + g.b_off + host_nest_offset(g.b_batch, bi);
         const uint64_t o_off = g.o_off + host_nest_offset(g.o_batch, bi);
         if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(b) % 16 != 0) return FB_ERR_UNSUPPORTED;
-        CUtensorMap ta, tb;
+        CUtensorMap ta, tb, tb_half;
         if (!make_2d_map(&ta, a, fmt, g.K, g.M, g.a_sm, BM)) return FB_ERR_UNSUPPORTED;
         if (b_mn ? !make_2d_map(&tb, b, fmt, g.N, g.K, g.b_sk, BK) : !make_2d_map(&tb, b, fmt, g.K, g.N, g.b_sn, (uint32_t)BN))
             return FB_ERR_UNSUPPORTED;
+        const bool half = BN == 256 && (b_mn ? (tb_half = tb, true) : make_2d_map(&tb_half, b, fmt, g.K, g.N, g.b_sn, BN / 2));
         ConvGemmParams p{};
         p.mode = 0;
         p.fmt = fmt;
@@ -513,12 +823,7 @@ int launch_gemm_tc(const GemmArgs& g, void* stream) {
         p.b_mn = b_mn ? 1 : 0;
         p.c_rows = g.o_sn == 1 && g.o_sm % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(g.out) + o_off * esz_out) % (4 * esz_out) == 0;
-        int r;
-        switch (BN) {
-            case 256: r = launch_bn<256>(ta, tb, p, st); break;
-            case 128: r = launch_bn<128>(ta, tb, p, st); break;
-            default: r = launch_bn<64>(ta, tb, p, st); break;
-        }
+        const int r = launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
         if (r != FB_OK) return r;
     }
     return FB_OK;
@@ -563,9 +868,10 @@ int launch_patches(const ConvArgs& a, void* stream) {
         if (cudaGetLastError() != cudaSuccess) return launch_status("weight gather");
         wptr = tmp;
     }
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tb_half;
     if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN) || !make_2d_map(&ta, pa, fmt, K, M, K, BM))
         return FB_ERR_UNSUPPORTED;
+    const bool half = BN == 256 && make_2d_map(&tb_half, wptr, fmt, K, O, K, BN / 2);
     ConvGemmParams p{};
     p.mode = 0;
     p.fmt = fmt;
@@ -586,11 +892,7 @@ int launch_patches(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
-    switch (BN) {
-        case 256: return launch_bn<256>(ta, tb, p, st);
-        case 128: return launch_bn<128>(ta, tb, p, st);
-        default: return launch_bn<64>(ta, tb, p, st);
-    }
+    return launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
 }
 
 int launch_conv_tc(const ConvArgs& a, void* stream) {
@@ -653,9 +955,10 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     const int BN = O % 256 == 0 ? 256 : O % 128 == 0 ? 128 : O % 64 == 0 ? 64 : 0;
     if (BN == 0) return FB_ERR_UNSUPPORTED;
 
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tb_half;
     const void* in_ptr = static_cast<const uint16_t*>(a.input) + a.in_offset;
     if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN)) return FB_ERR_UNSUPPORTED;
+    const bool half = BN == 256 && make_2d_map(&tb_half, wptr, fmt, K, O, K, BN / 2);
     ConvGemmParams p{};
     if (one_by_one) {
         if (!make_2d_map(&ta, in_ptr, fmt, C, M, C, BM)) return FB_ERR_UNSUPPORTED;
@@ -689,11 +992,7 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
-    switch (BN) {
-        case 256: return launch_bn<256>(ta, tb, p, st);
-        case 128: return launch_bn<128>(ta, tb, p, st);
-        default: return launch_bn<64>(ta, tb, p, st);
-    }
+    return launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
 }
 
 }  // namespace fb
