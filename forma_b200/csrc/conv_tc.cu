@@ -321,22 +321,27 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
 // loads of a stage have landed on the even CTA's `full` barrier, and its
 // commits arrive on both CTAs' `empty` / `tfull` barriers; both epilogues
 // arrive on the even CTA's `tempty`.
+// BN (256 or 192) is the pair tile's N: each CTA loads BN / 2 rows of B, and
+// 192 fits tile counts of N = 768 / 2304 / 3072 to 74 pairs better than 256.
+template <int BN_>
 struct PairCfg {
-    static constexpr int BN = 256;                 // pair tile N; each CTA loads BN / 2 rows of B
-    static constexpr int A_BYTES = BM * BK * 2;    // 16 KB
-    static constexpr int B_BYTES = BN / 2 * BK * 2;  // 16 KB
+    static constexpr int BN = BN_;
+    static constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+    static constexpr int B_BYTES = BN / 2 * BK * 2;  // 16 KB (256) / 12 KB (192)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = 6;
-    static constexpr int TMEM_COLS = 512;          // two 256-column accumulators
+    static constexpr int STAGES = BN == 256 ? 6 : 7;
+    static constexpr int TMEM_COLS = 512;            // two BN-column accumulators
     static constexpr int EPI_PITCH = 36;
     static constexpr int EPI_BYTES = 4 * 32 * EPI_PITCH * 4;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
+    static_assert(SMEM <= 227 * 1024, "pair configuration exceeds shared memory");
 };
 
+template <int BN_>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     conv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           ConvGemmParams p) {
-    using C = PairCfg;
+    using C = PairCfg<BN_>;
     constexpr int BN = C::BN;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -410,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     tma_load_im2col_4d_pair(a_dst, &tmA, (int32_t)(cb * BK), w0, h0, n0, (uint16_t)(s * p.dil_w),
                                             (uint16_t)(r * p.dil_h), bar);
                 }
-                if (p.b_mn) {
+                if (BN % 128 == 0 && p.b_mn) {  // MN-major B in 64-column blocks (host: BN = 256 only)
 #pragma unroll
                     for (int nb = 0; nb < BN / 2 / 64; ++nb)
                         tma_load_2d_pair(b_dst + nb * (BK * 128), &tmB, b0 + nb * 64, (int32_t)(kb * BK), bar);
@@ -451,7 +456,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 }
                 tc_fence_after();
                 const uint64_t ad = sw128_desc(smem_u32(ring + stage * C::STAGE_BYTES));
-                if (p.b_mn) {
+                if (BN % 128 == 0 && p.b_mn) {
                     const uint64_t bd = sw128_mn_desc(smem_u32(ring + stage * C::STAGE_BYTES + C::A_BYTES), BK * 128);
                     umma_f16_ss_pair_warp(d, ad, bd, idesc_mn, kb != 0);
 #pragma unroll
@@ -698,47 +703,94 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams
     return launch_status("kernel launch");
 }
 
-// CTA-pair launch for N a multiple of 256 and at least two 128-row M tiles;
-// `tb_half` boxes 128 rows of K-major B (MN-major B: the usual 64 x BK box).
-// FB_ERR_UNSUPPORTED when no 2-CTA cluster can be resident.
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, const ConvGemmParams& p, cudaStream_t st) {
-    if (p.m_tiles < 2) return FB_ERR_UNSUPPORTED;
-    if (cudaFuncSetAttribute(conv_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM) !=
-        cudaSuccess)
-        return launch_status("shared-memory attribute");
-    static int max_clusters[64] = {0};
+// The B operand of a launch: [N, K] rows with K contiguous, or (mn) [K, N]
+// rows with N contiguous; `pitch` is the row pitch in elements.
+struct BOperand {
+    const void* ptr;
+    uint32_t fmt;
+    uint64_t k, n, pitch;
+    bool mn;
+};
+
+bool make_b_map(CUtensorMap* m, const BOperand& b, uint32_t box_n) {
+    return b.mn ? make_2d_map(m, b.ptr, b.fmt, b.n, b.k, b.pitch, BK) : make_2d_map(m, b.ptr, b.fmt, b.k, b.n, b.pitch, box_n);
+}
+
+// 2-CTA clusters of the pair kernel that can be resident at once (0: none).
+template <int BN>
+int pair_clusters() {
+    static int cached[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (max_clusters[dev] == 0) {
+    if (cached[dev] == 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (unsigned)sm_count());
         cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        cfg.dynamicSmemBytes = PairCfg<BN>::SMEM;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, conv_gemm_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+        if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PairCfg<BN>::SMEM) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&n, conv_gemm_pair_kernel<BN>, &cfg) != cudaSuccess || n < 1) {
             (void)cudaGetLastError();
-            max_clusters[dev] = -1;
-        } else {
-            max_clusters[dev] = n;
+            n = -1;
         }
+        cached[dev] = n;
     }
-    if (max_clusters[dev] < 1) return FB_ERR_UNSUPPORTED;
+    return cached[dev] > 0 ? cached[dev] : 0;
+}
+
+template <int BN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, const ConvGemmParams& p, int clusters_max,
+                cudaStream_t st) {
+    if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PairCfg<BN>::SMEM) != cudaSuccess)
+        return launch_status("shared-memory attribute");
     const uint32_t tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
-    const uint32_t clusters = tiles < (uint32_t)max_clusters[dev] ? tiles : (uint32_t)max_clusters[dev];
-    conv_gemm_pair_kernel<<<2 * clusters, THREADS, PairCfg::SMEM, st>>>(ta, tb_half, p);
+    const uint32_t clusters = tiles < (uint32_t)clusters_max ? tiles : (uint32_t)clusters_max;
+    conv_gemm_pair_kernel<BN><<<2 * clusters, THREADS, PairCfg<BN>::SMEM, st>>>(ta, tb_half, p);
     count_launch();
     return launch_status("kernel launch");
 }
 
-// Dispatch by tile width: CTA pairs for BN = 256 when a half-width B map is
-// given, else one CTA per tile.
-int launch_tiles(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tb_half,
-                 const ConvGemmParams& p, cudaStream_t st) {
-    if (BN == 256 && tb_half) {
-        const int r = launch_pair(ta, *tb_half, p, st);
-        if (r != FB_ERR_UNSUPPORTED) return r;
+// Tile shape and kernel for one GEMM launch (p.n_tiles is set here).  CTA
+// pairs when N is a multiple of 256 or (K-major B) 192 and there are at least
+// two 128-row M tiles: the width with the fewest tile-rounds x width wins
+// (ties to 256, fewer re-reads of A).  Otherwise one CTA per 128 x BN tile
+// with the widest BN in {256, 128, 64} dividing N.  FB_ERR_UNSUPPORTED when
+// N is not a multiple of 64.
+int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cudaStream_t st) {
+    const uint64_t N = b.n;
+    if (p.m_tiles >= 2) {
+        const uint64_t m_pairs = (p.m_tiles + 1) / 2;
+        int best = 0;
+        uint64_t best_cost = ~0ull;
+        int best_clusters = 0;
+        for (int bn : {256, 192}) {
+            if (N % bn != 0 || (b.mn && bn != 256)) continue;
+            const int cl = bn == 256 ? pair_clusters<256>() : pair_clusters<192>();
+            if (cl == 0) continue;
+            const uint64_t tiles = m_pairs * (N / bn);
+            const uint64_t cost = (tiles + cl - 1) / cl * bn;
+            if (cost < best_cost) {
+                best_cost = cost;
+                best = bn;
+                best_clusters = cl;
+            }
+        }
+        if (best) {
+            CUtensorMap tb;
+            if (!make_b_map(&tb, b, (uint32_t)best / 2)) return FB_ERR_UNSUPPORTED;
+            p.n_tiles = (uint32_t)(N / best);
+            return best == 256 ? launch_pair<256>(ta, tb, p, best_clusters, st)
+                               : launch_pair<192>(ta, tb, p, best_clusters, st);
+        }
     }
+    const int BN = N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : N % 64 == 0 ? 64 : 0;
+    if (BN == 0) return FB_ERR_UNSUPPORTED;
+    CUtensorMap tb;
+    if (!make_b_map(&tb, b, (uint32_t)BN)) return FB_ERR_UNSUPPORTED;
+    p.n_tiles = (uint32_t)(N / BN);
     switch (BN) {
         case 256: return launch_bn<256>(ta, tb, p, st);
         case 128: return launch_bn<128>(ta, tb, p, st);
@@ -797,11 +849,9 @@ int launch_gemm_tc(const GemmArgs& g, void* stream) {
         const uint16_t* b = static_cast<const uint16_t*>(g.b) + g.b_off + host_nest_offset(g.b_batch, bi);
         const uint64_t o_off = g.o_off + host_nest_offset(g.o_batch, bi);
         if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(b) % 16 != 0) return FB_ERR_UNSUPPORTED;
-        CUtensorMap ta, tb, tb_half;
+        CUtensorMap ta;
         if (!make_2d_map(&ta, a, fmt, g.K, g.M, g.a_sm, BM)) return FB_ERR_UNSUPPORTED;
-        if (b_mn ? !make_2d_map(&tb, b, fmt, g.N, g.K, g.b_sk, BK) : !make_2d_map(&tb, b, fmt, g.K, g.N, g.b_sn, (uint32_t)BN))
-            return FB_ERR_UNSUPPORTED;
-        const bool half = BN == 256 && (b_mn ? (tb_half = tb, true) : make_2d_map(&tb_half, b, fmt, g.K, g.N, g.b_sn, BN / 2));
+        const BOperand bop{b, fmt, g.K, g.N, b_mn ? g.b_sk : g.b_sn, b_mn};
         ConvGemmParams p{};
         p.mode = 0;
         p.fmt = fmt;
@@ -812,7 +862,6 @@ int launch_gemm_tc(const GemmArgs& g, void* stream) {
         p.S = 1;
         p.stride_h = p.stride_w = p.dil_h = p.dil_w = 1;
         p.m_tiles = (uint32_t)((g.M + BM - 1) / BM);
-        p.n_tiles = (uint32_t)(g.N / BN);
         p.out = static_cast<float*>(g.out);
         p.out_offset = o_off;
         p.s_n = 0;
@@ -823,7 +872,7 @@ int launch_gemm_tc(const GemmArgs& g, void* stream) {
         p.b_mn = b_mn ? 1 : 0;
         p.c_rows = g.o_sn == 1 && g.o_sm % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(g.out) + o_off * esz_out) % (4 * esz_out) == 0;
-        const int r = launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
+        const int r = launch_tiles(ta, bop, p, st);
         if (r != FB_OK) return r;
     }
     return FB_OK;
@@ -868,10 +917,9 @@ int launch_patches(const ConvArgs& a, void* stream) {
         if (cudaGetLastError() != cudaSuccess) return launch_status("weight gather");
         wptr = tmp;
     }
-    CUtensorMap ta, tb, tb_half;
-    if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN) || !make_2d_map(&ta, pa, fmt, K, M, K, BM))
-        return FB_ERR_UNSUPPORTED;
-    const bool half = BN == 256 && make_2d_map(&tb_half, wptr, fmt, K, O, K, BN / 2);
+    CUtensorMap ta;
+    if (!make_2d_map(&ta, pa, fmt, K, M, K, BM)) return FB_ERR_UNSUPPORTED;
+    const BOperand bop{wptr, fmt, K, O, K, false};
     ConvGemmParams p{};
     p.mode = 0;
     p.fmt = fmt;
@@ -883,7 +931,6 @@ int launch_patches(const ConvArgs& a, void* stream) {
     p.S = 1;
     p.stride_h = p.stride_w = p.dil_h = p.dil_w = 1;
     p.m_tiles = (uint32_t)((M + BM - 1) / BM);
-    p.n_tiles = (uint32_t)(O / BN);
     p.out = a.output;
     p.out_offset = a.out_offset;
     p.s_n = a.out_stride_n;
@@ -892,7 +939,7 @@ int launch_patches(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
-    return launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
+    return launch_tiles(ta, bop, p, st);
 }
 
 int launch_conv_tc(const ConvArgs& a, void* stream) {
@@ -955,10 +1002,9 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     const int BN = O % 256 == 0 ? 256 : O % 128 == 0 ? 128 : O % 64 == 0 ? 64 : 0;
     if (BN == 0) return FB_ERR_UNSUPPORTED;
 
-    CUtensorMap ta, tb, tb_half;
+    CUtensorMap ta;
     const void* in_ptr = static_cast<const uint16_t*>(a.input) + a.in_offset;
-    if (!make_2d_map(&tb, wptr, fmt, K, O, K, (uint32_t)BN)) return FB_ERR_UNSUPPORTED;
-    const bool half = BN == 256 && make_2d_map(&tb_half, wptr, fmt, K, O, K, BN / 2);
+    const BOperand bop{wptr, fmt, K, O, K, false};
     ConvGemmParams p{};
     if (one_by_one) {
         if (!make_2d_map(&ta, in_ptr, fmt, C, M, C, BM)) return FB_ERR_UNSUPPORTED;
@@ -983,7 +1029,6 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.dil_h = (int32_t)a.dilation[0];
     p.dil_w = (int32_t)a.dilation[1];
     p.m_tiles = (uint32_t)((M + BM - 1) / BM);
-    p.n_tiles = (uint32_t)(O / BN);
     p.out = a.output;
     p.out_offset = a.out_offset;
     p.s_n = a.out_stride_n;
@@ -992,7 +1037,7 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
-    return launch_tiles(BN, ta, tb, half ? &tb_half : nullptr, p, st);
+    return launch_tiles(ta, bop, p, st);
 }
 
 }  // namespace fb
