@@ -91,6 +91,8 @@ SIGNATURES = {
     "fb_conv": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
     "fb_conv_low_f32": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
     "fb_conv_low": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
+    "fb_conv_low_gelu": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
+    "fb_conv_low_f32_accumulate": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
     "fb_attention_plan": (
         C.c_int,
         [U64P, C.c_uint32, U64P, C.c_uint32, U64P, C.c_uint32, U64P, C.c_uint32, FbAttentionOptions, U64P, U32P],

@@ -242,6 +242,26 @@ def conv_low_into(input, weight, options, out):
     return out
 
 
+def conv_low_gelu_into(input, weight, options, out):
+    """gelu_to_low(conv_low_f32(input, weight)) into a 16-bit output view, the
+    GELU applied in the tensor-core GEMM's epilogue (bit-identical)."""
+    dev = _device(input, weight)
+    opts, _keep = _conv_options(options)
+    di, dw, do = describe(input), describe(weight), describe(out)
+    _check(lib().fb_conv_low_gelu(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    return out
+
+
+def conv_low_f32_accumulate(input, weight, options, out):
+    """out += conv_low_f32(input, weight) in place (f32 output view): a
+    residual connection folded into the GEMM epilogue (bit-identical to add)."""
+    dev = _device(input, weight)
+    opts, _keep = _conv_options(options)
+    di, dw, do = describe(input), describe(weight), describe(out)
+    _check(lib().fb_conv_low_f32_accumulate(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    return out
+
+
 # ------------------------------------------------------- low-precision GEMM
 
 def matmul_plan(left_shape: Sequence[int], right_shape: Sequence[int]) -> list:

@@ -300,8 +300,28 @@ ConvArgs conv_args(const View& in, const View& w, const View& res, const ConvPla
     return a;
 }
 
+// True when the view's elements fill a dense block in some axis order (a
+// contiguous tensor or a permuted view of one, e.g. channels-last).
+bool dense_permutation(const View& v) {
+    std::vector<std::pair<uint64_t, uint64_t>> ax;
+    for (size_t i = 0; i < v.dims.size(); ++i)
+        if (v.dims[i] > 1) ax.push_back({v.strides[i], v.dims[i]});
+    std::sort(ax.begin(), ax.end());
+    uint64_t expect = 1;
+    for (auto& e : ax) {
+        if (e.first != expect) return false;
+        expect *= e.second;
+    }
+    return true;
+}
+
+// Epilogues of the glue entry points: none, GELU before the low rounding
+// (fb_conv_low_gelu), or accumulation into the f32 output
+// (fb_conv_low_f32_accumulate).
+enum ConvEpilogue : uint32_t { CONV_EPI_NONE = 0, CONV_EPI_GELU = 1, CONV_EPI_ACCUMULATE = 2 };
+
 int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
-              void* stream, bool low, bool round_low) {
+              void* stream, bool low, bool round_low, uint32_t epi = CONV_EPI_NONE) {
     View in, w, out;
     FB_TRY(view_of(input, "input", &in));
     FB_TRY(view_of(weight, "weight", &w));
@@ -330,29 +350,44 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
             if (v > 0xffffffffull) return fail(FB_ERR_INVALID_INPUT, "CUDA convolution coordinate exceeds u32");
 
     // conv_low on the tensor-core path rounds in the GEMM epilogue and writes
-    // the 16-bit output directly; every other path computes an f32 result
-    // (in scratch for conv_low) and rounds it in a separate pass.
-    if (round_low && in.count > 0 && plan.channels_per_group > 0) {
+    // the 16-bit output directly (the GELU and accumulate epilogues likewise
+    // act on the f32 sums there); every other path computes an f32 result
+    // (in scratch for conv_low and the epilogues) and finishes it in a
+    // separate pass.
+    const bool via_scratch = round_low || epi == CONV_EPI_ACCUMULATE;
+    if (via_scratch && in.count > 0 && plan.channels_per_group > 0) {
         ConvArgs d = conv_args(in, w, out, plan);
         d.output = static_cast<float*>(out.data);
-        d.out_low = out.dtype;
+        d.out_low = round_low ? out.dtype : 0;
+        d.act = epi == CONV_EPI_GELU ? 1 : 0;
+        d.accumulate = epi == CONV_EPI_ACCUMULATE ? 1 : 0;
         const int st = launch_conv_tc(d, stream);
         if (st != FB_ERR_UNSUPPORTED) return launched(st, "convolution");
     }
-    // f32 result buffer: the output itself, or scratch before low rounding.
+    if (epi == CONV_EPI_ACCUMULATE && (in.count == 0 || plan.channels_per_group == 0)) return FB_OK;  // adds zeros
+    // f32 result buffer: the output itself, or scratch before the finishing
+    // pass.  The scratch copy takes the output's own memory order when that
+    // is a dense block (contiguous or permuted, e.g. channels-last), so the
+    // finishing pass maps memory position to memory position.
     float* result = nullptr;
     View res = out;
-    if (round_low) {
+    const bool out_dense = dense_permutation(out);
+    if (round_low && !out_dense) return fail(FB_ERR_INVALID_INPUT, "low convolution output must be a dense block");
+    if (via_scratch) {
         result = static_cast<float*>(scratch(stream, out.count * 4 + 256, SCRATCH_CONV_RESULT));
         if (!result) return fail(FB_ERR_DRIVER, "scratch allocation failed");
         res.data = result;
         res.offset = 0;
         res.dtype = FB_F32;
-        res.strides.assign(res.dims.size(), 0);
-        uint64_t s = 1;
-        for (size_t i = res.dims.size(); i-- > 0;) {
-            res.strides[i] = s;
-            s *= res.dims[i];
+        if (out_dense) {
+            res.strides = out.strides;
+        } else {
+            res.strides.assign(res.dims.size(), 0);
+            uint64_t s = 1;
+            for (size_t i = res.dims.size(); i-- > 0;) {
+                res.strides[i] = s;
+                s *= res.dims[i];
+            }
         }
     }
     if (in.count == 0 || plan.channels_per_group == 0) {
@@ -369,11 +404,23 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
         s = launched(s, "convolution");
         if (s != FB_OK) return s;
     }
-    if (round_low) {
+    if (epi == CONV_EPI_ACCUMULATE) {
+        // output += result (the output is its own first operand)
+        float* o = static_cast<float*>(out.data);
+        Nest on = make_nest(out.dims, out.strides, all_axes(out.dims.size()));
         Nest rn = make_nest(res.dims, res.strides, all_axes(res.dims.size()));
-        // Output must be contiguous for the cast (cast_to_low writes dense).
-        if (!is_contiguous(out)) return fail(FB_ERR_INVALID_INPUT, "low convolution output must be contiguous");
-        return launched(launch_cast_to_low(result, 0, rn, static_cast<uint16_t*>(out.data) + out.offset, out.dtype,
+        const bool dense = is_contiguous(out) && out.count % 4 == 0 && reinterpret_cast<uintptr_t>(o + out.offset) % 16 == 0 &&
+                           reinterpret_cast<uintptr_t>(result) % 16 == 0;
+        return launched(launch_add(o, out.offset, on, result, 0, rn, o, out.offset, on, out.count, dense, stream), "add");
+    }
+    if (round_low) {
+        // scratch and output share one memory order: a dense position-wise pass
+        Nest flat = make_nest(Dims{out.count}, Dims{1}, all_axes(1));
+        if (epi == CONV_EPI_GELU)
+            return launched(launch_gelu_to_low(result, 0, flat, static_cast<uint16_t*>(out.data) + out.offset, out.dtype,
+                                               out.count, stream),
+                            "gelu");
+        return launched(launch_cast_to_low(result, 0, flat, static_cast<uint16_t*>(out.data) + out.offset, out.dtype,
                                            out.count, stream),
                         "cast");
     }
@@ -722,6 +769,16 @@ int fb_conv_low_f32(const fb_tensor* input, const fb_tensor* weight, const fb_co
 int fb_conv_low(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
                 void* stream) {
     return conv_impl(input, weight, options, output, stream, true, true);
+}
+
+int fb_conv_low_gelu(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
+                     void* stream) {
+    return conv_impl(input, weight, options, output, stream, true, true, CONV_EPI_GELU);
+}
+
+int fb_conv_low_f32_accumulate(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options,
+                               fb_tensor* output, void* stream) {
+    return conv_impl(input, weight, options, output, stream, true, false, CONV_EPI_ACCUMULATE);
 }
 
 int fb_attention_plan(const uint64_t* q_dims, uint32_t q_rank, const uint64_t* k_dims, uint32_t k_rank,

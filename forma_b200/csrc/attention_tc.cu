@@ -2,7 +2,8 @@
 //
 // attention_low_f32 for 16-bit Q/K/V, depth D in {64, 128}, keep / additive
 // masks, optional causal offset.  One CTA owns 256 query rows (two 128-row Q
-// tiles) of one (batch, head) and streams that head's K/V once for both tiles.
+// tiles) of one (batch, head) and streams that head's K/V once for both tiles
+// (short key ranges at depth 64: one Q tile per CTA, two CTAs per SM).
 //   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128
 //               keys into rings of 2 (D = 128) or 4 (D = 64) slots with their
 //               own full/empty barriers (128B-swizzled boxes of 64 depth
@@ -52,7 +53,7 @@ namespace {
 
 __device__ uint32_t g_attn_status;
 
-constexpr int TQ = 128, TK = 128, QT = 2, THREADS = 64 + QT * 128;
+constexpr int TQ = 128, TK = 128;
 
 struct AttnParams {
     uint32_t fmt;           // 0 f16, 1 bf16
@@ -70,19 +71,24 @@ struct AttnParams {
     uint64_t m_sb, m_sh, m_sq;              // mask strides (elements; 0 = broadcast) of batch, head, query
 };
 
-template <int D>
+// QT Q tiles of 128 rows per CTA: 2 (the two tiles' softmax and MMA
+// ping-pong on one SM) or 1 (short key ranges at D = 64: 256 TMEM columns and
+// two K/V stages, so two CTAs share an SM and overlap each other's load and
+// epilogue latency).
+template <int D, int QT>
 struct ACfg {
+    static constexpr int THREADS = 64 + QT * 128;
     static constexpr int BOXES = D / 64;               // 64-column swizzle boxes per row
     static constexpr int Q_BYTES = TQ * D * 2;         // one Q tile
     static constexpr int K_BYTES = TK * D * 2;
     static constexpr int V_BYTES = TK * D * 2;
     static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-    static constexpr int STAGES = D == 64 ? 4 : 2;
+    static constexpr int STAGES = QT == 1 ? 2 : D == 64 ? 4 : 2;
     static constexpr int SMEM = 1024 + QT * Q_BYTES + STAGES * STAGE_BYTES + 256;
-    static constexpr uint32_t TMEM_COLS = 512;
-    // TMEM columns: S_t at t*128 (P_t aliases its first 64), O_t at 256 + t*128.
+    static constexpr uint32_t TMEM_COLS = QT == 1 ? 256 : 512;
+    // TMEM columns: S_t at t*128 (P_t aliases its first 64), O_t at QT*128 + t*128.
     static __device__ __forceinline__ uint32_t s_col(int t) { return (uint32_t)(t * TK); }
-    static __device__ __forceinline__ uint32_t o_col(int t) { return (uint32_t)(2 * TK + t * 128); }
+    static __device__ __forceinline__ uint32_t o_col(int t) { return (uint32_t)(QT * TK + t * 128); }
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -173,11 +179,11 @@ __device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t 
 // MASK: FB_MASK_NONE, FB_MASK_KEEP (u32, nonzero keeps the key) or
 // FB_MASK_ADDITIVE (f32 added to the scaled score; -inf excludes the key), as
 // the reference applies them (compute-cuda/src/attention.cu:55-80).
-template <int D, int MASK>
-__global__ void __launch_bounds__(THREADS, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+template <int D, int MASK, int QT>
+__global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV, AttnParams p) {
-    using C = ACfg<D>;
+    using C = ACfg<D, QT>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sQ = smem;                          // QT tiles
@@ -592,10 +598,10 @@ bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t D, 
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D>
+template <int D, int QT>
 int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLayout& kl, const RowsLayout& vl,
              const RowsLayout& ol, const RowsLayout& ml, cudaStream_t st) {
-    using C = ACfg<D>;
+    using C = ACfg<D, QT>;
     const int r = (int)a.row_rank;
     const uint64_t L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
     const uint64_t BH = a.rows / L;
@@ -634,15 +640,15 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     p.m_sb = ml.s_batch;
     p.m_sh = ml.s_head;
     p.m_sq = ml.s_row;
-    auto kernel = a.mask_kind == FB_MASK_KEEP       ? attn_fwd_kernel<D, FB_MASK_KEEP>
-                  : a.mask_kind == FB_MASK_ADDITIVE ? attn_fwd_kernel<D, FB_MASK_ADDITIVE>
-                                                    : attn_fwd_kernel<D, FB_MASK_NONE>;
+    auto kernel = a.mask_kind == FB_MASK_KEEP       ? attn_fwd_kernel<D, FB_MASK_KEEP, QT>
+                  : a.mask_kind == FB_MASK_ADDITIVE ? attn_fwd_kernel<D, FB_MASK_ADDITIVE, QT>
+                                                    : attn_fwd_kernel<D, FB_MASK_NONE, QT>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return launch_status("shared-memory attribute");
     const uint64_t grid = (uint64_t)p.q_blocks * BH;
     if (grid == 0) return FB_OK;
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
-    kernel<<<(unsigned)grid, THREADS, C::SMEM, st>>>(tq, tk, tv, p);
+    kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
     count_launch();
     return launch_status("kernel launch");
 }
@@ -701,7 +707,14 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
         return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return D == 64 ? launch_d<64>(a, fmt, ql, kl, vl, ol, ml, st) : launch_d<128>(a, fmt, ql, kl, vl, ol, ml, st);
+    // Short key ranges at D = 64 (the whole K/V loop is a few tiles, so each
+    // CTA's fixed load and epilogue latency dominates): one Q tile per CTA,
+    // two CTAs per SM.
+    if (D == 64) {
+        return Lk <= 4 * TK ? launch_d<64, 1>(a, fmt, ql, kl, vl, ol, ml, st)
+                            : launch_d<64, 2>(a, fmt, ql, kl, vl, ol, ml, st);
+    }
+    return launch_d<128, 2>(a, fmt, ql, kl, vl, ol, ml, st);
 }
 
 }  // namespace fb

@@ -47,6 +47,8 @@ struct ConvGemmParams {
     uint32_t c_rows;  // 1: channels contiguous (s_c == 1) and aligned rows (16 B for f32, 8 B for 16-bit)
     uint32_t b_mn;    // 0: B map is [N, K] (K contiguous); 1: B map is [K, N] (N contiguous, MN-major operand)
     uint32_t out_low; // 0: f32 output; FB_BF16 / FB_F16: rounded once (nearest even) to that type
+    uint32_t act;     // 1: tanh GELU of each f32 sum before the store / rounding
+    uint32_t accumulate;  // 1: f32 output += sum (read-modify-write)
     float* out;       // f32 output, or the 16-bit output's storage when out_low != 0
     uint64_t out_offset, s_n, s_c, s_p, s_q;
 };
@@ -254,6 +256,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
+                    if (p.act) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_tanh(__uint_as_float(v[j])));
+                    }
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
                         *reinterpret_cast<float4*>(st + lane * C::EPI_PITCH + 4 * q) =
@@ -270,7 +276,11 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                                 *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
                                     make_uint2(encode_low_pair(val.x, val.y, p.out_low),
                                                encode_low_pair(val.z, val.w, p.out_low));
-                            else
+                            else if (p.accumulate) {
+                                float4* o = reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc);
+                                const float4 prev = *o;
+                                *o = make_float4(prev.x + val.x, prev.y + val.y, prev.z + val.z, prev.w + val.w);
+                            } else
                                 *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
                         }
                     }
@@ -282,6 +292,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
+                    if (p.act) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_tanh(__uint_as_float(v[j])));
+                    }
                     if (base != ~0ull) {
                         if (p.out_low == FB_BF16) {
 #pragma unroll
@@ -291,6 +305,9 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
 #pragma unroll
                             for (int j = 0; j < 32; ++j)
                                 out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_f16(__uint_as_float(v[j]));
+                        } else if (p.accumulate) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] += __uint_as_float(v[j]);
                         } else {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
@@ -516,6 +533,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
+                    if (p.act) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_tanh(__uint_as_float(v[j])));
+                    }
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
                         *reinterpret_cast<float4*>(st + lane * C::EPI_PITCH + 4 * q) =
@@ -532,7 +553,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                 *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
                                     make_uint2(encode_low_pair(val.x, val.y, p.out_low),
                                                encode_low_pair(val.z, val.w, p.out_low));
-                            else
+                            else if (p.accumulate) {
+                                float4* o = reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc);
+                                const float4 prev = *o;
+                                *o = make_float4(prev.x + val.x, prev.y + val.y, prev.z + val.z, prev.w + val.w);
+                            } else
                                 *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
                         }
                     }
@@ -544,6 +569,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
+                    if (p.act) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_tanh(__uint_as_float(v[j])));
+                    }
                     if (base != ~0ull) {
                         if (p.out_low == FB_BF16) {
 #pragma unroll
@@ -553,6 +582,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
                             for (int j = 0; j < 32; ++j)
                                 out16[base + (uint64_t)(c0 + j) * p.s_c] = encode_f16(__uint_as_float(v[j]));
+                        } else if (p.accumulate) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] += __uint_as_float(v[j]);
                         } else {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) p.out[base + (uint64_t)(c0 + j) * p.s_c] = __uint_as_float(v[j]);
@@ -939,6 +971,8 @@ int launch_patches(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
+    p.act = a.act;
+    p.accumulate = a.accumulate;
     return launch_tiles(ta, bop, p, st);
 }
 
@@ -1037,6 +1071,8 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
     p.s_q = a.out_strides[1];
     p.c_rows = c_rows_ok(a) ? 1 : 0;
     p.out_low = a.out_low;
+    p.act = a.act;
+    p.accumulate = a.accumulate;
     return launch_tiles(ta, bop, p, st);
 }
 

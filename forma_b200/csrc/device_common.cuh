@@ -99,6 +99,15 @@ __device__ __forceinline__ uint32_t encode_low_pair(float lo, float hi, uint32_t
                             : (uint32_t)encode_f16(lo) | ((uint32_t)encode_f16(hi) << 16);
 }
 
+// tanh form of GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), as
+// x / (1 + exp(-2u)): the same value without the cancellation of 1 + tanh
+// for large negative x.
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    const float u = k0 * fmaf(k1 * x, x * x, x);
+    return x / (1.0f + expf(-2.0f * u));
+}
+
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
     for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);

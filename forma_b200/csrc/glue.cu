@@ -41,12 +41,6 @@ __global__ void add_dense_kernel(const float4* a, const float4* b, float4* out, 
 // the sum 1 + tanh(u) cancels catastrophically in f32 for u below about -4,
 // the quotient keeps full relative precision (and is exactly -0 once exp
 // overflows, where the f64 form also rounds to zero).
-__device__ __forceinline__ float gelu_tanh(float x) {
-    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-    const float u = k0 * fmaf(k1 * x, x * x, x);
-    return x / (1.0f + expf(-2.0f * u));
-}
-
 __global__ void gelu_to_low_kernel(const float* in, uint64_t in_off, Nest n, uint16_t* out, uint32_t dtype,
                                    uint64_t count) {
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {

@@ -148,6 +148,11 @@ struct ConvArgs {
     // and the result is rounded once (conv_low); only the tensor-core path
     // accepts this, the others return FB_ERR_UNSUPPORTED for it.
     uint32_t out_low = 0;
+    // Epilogue of the tensor-core path (the others return FB_ERR_UNSUPPORTED
+    // when either is set): act 1 applies the tanh GELU to each f32 sum before
+    // it is stored or rounded; accumulate 1 adds each f32 sum to the f32
+    // output already in memory (output += conv).
+    uint32_t act = 0, accumulate = 0;
 };
 int launch_conv_direct(const ConvArgs& a, void* stream);
 // Returns FB_ERR_UNSUPPORTED when the geometry has no tiled kernel.

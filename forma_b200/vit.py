@@ -9,15 +9,18 @@ joined by residual additions and a GELU.  Pre-norm blocks::
     for each layer:
         h  = LN(x)                                     layer_norm, eps 1e-5, rounded to BF16 as stored
         q, k, v = heads(h W_qkv)                       1x1 conv rounded to BF16 in its epilogue
-        x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv
+        x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv adding into x
         h  = LN(x)
-        x  = x + GELU(h W_1) W_2                        1x1 convs
+        x  = x + GELU(h W_1) W_2                        1x1 convs: GELU and rounding in the first's
+                                                       epilogue, the second adding into x
 
 Tokens live as a channels-last [B, 1, L, E] map, so every projection is a
 1x1 convolution whose input rows are the tokens (the tensor-core implicit
-GEMM reads them in place) and whose f32 result is written channels-last
-through a permuted output view.  Operands of the contractions are rounded
-to the low dtype at the points marked by the casts; everything else is f32.
+GEMM reads them in place) and whose result is written channels-last through
+a permuted output view.  The GELU and the residual additions are applied to
+the GEMM's f32 sums in its epilogue (the same arithmetic as the separate
+glue kernels, so the results are identical); operands of the contractions
+are rounded to the low dtype at the marked points; everything else is f32.
 Weights are random (seeded); no checkpoint is involved.
 """
 
@@ -30,6 +33,8 @@ import torch
 
 from . import api
 from .api import AttentionOptions, ConvOptions
+
+_ONE = ConvOptions([1, 1], [1, 1], [0, 0], [0, 0])  # 1x1, stride 1, no padding
 
 
 @dataclass(frozen=True)
@@ -114,18 +119,21 @@ class ViTEncoder:
             "qkv_low": torch.empty(B, 1, L, 3 * E, dtype=low, device=dev),   # [B, L, 3, H, D] rounded once
             "a": torch.empty(B, L, E, device=dev),                          # attention output, [B, L, H, D] order
             "a_low": torch.empty(B, L, E, dtype=low, device=dev),
-            "o": torch.empty(B, 1, L, E, device=dev),
-            "m": torch.empty(B, 1, L, M, device=dev),
             "m_low": torch.empty(B, 1, L, M, dtype=low, device=dev),
         }
         return self._bufs
 
     @staticmethod
-    def _proj(x_low: torch.Tensor, weight: torch.Tensor, out: torch.Tensor) -> None:
-        """1x1 convolution of channels-last tokens [B, L, Cin] into out [B, 1, L, Cout] (f32)."""
+    def _tokens(x_low: torch.Tensor) -> torch.Tensor:
+        """Channels-last tokens [B, L, C] as the logical [B, C, 1, L] input of a 1x1 convolution."""
         B, L, Cin = x_low.shape
-        xin = x_low.view(B, 1, L, Cin).permute(0, 3, 1, 2)  # logical [B, Cin, 1, L], channels-last storage
-        api.conv_low_f32_into(xin, weight, ConvOptions([1, 1], [1, 1], [0, 0], [0, 0]), out.permute(0, 3, 1, 2))
+        return x_low.view(B, 1, L, Cin).permute(0, 3, 1, 2)
+
+    @staticmethod
+    def _residual(x_low: torch.Tensor, weight: torch.Tensor, x: torch.Tensor) -> None:
+        """x [B, L, E] (f32) += 1x1 convolution of channels-last tokens x_low [B, L, Cin]."""
+        B, L, E = x.shape
+        api.conv_low_f32_accumulate(ViTEncoder._tokens(x_low), weight, _ONE, x.view(B, 1, L, E).permute(0, 3, 1, 2))
 
     def forward(self, img: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
@@ -145,19 +153,15 @@ class ViTEncoder:
             api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])  # rounded as stored
             # QKV rounded once in the GEMM epilogue (conv_low), read by the
             # attention kernel as head-interleaved views of one buffer
-            xin = b["h_low"].view(B, 1, L, E).permute(0, 3, 1, 2)
-            api.conv_low_into(xin, blk["qkv"], ConvOptions([1, 1], [1, 1], [0, 0], [0, 0]),
-                              b["qkv_low"].permute(0, 3, 1, 2))
+            api.conv_low_into(self._tokens(b["h_low"]), blk["qkv"], _ONE, b["qkv_low"].permute(0, 3, 1, 2))
             qkv = b["qkv_low"].view(B, L, 3, H, D)
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))   # [B, H, L, D] views
             api.attention_low_f32_into(q, k, v, None, opts, b["a"].view(B, L, H, D).permute(0, 2, 1, 3))
             api.cast_to_low_into(b["a"], b["a_low"])
-            self._proj(b["a_low"], blk["proj"], b["o"])
-            api.add(x, b["o"].view(B, L, E), out=x)
+            self._residual(b["a_low"], blk["proj"], x)                  # x += proj (GEMM epilogue)
             # MLP sub-block
             api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])
-            self._proj(b["h_low"], blk["fc1"], b["m"])
-            api.gelu_to_low(b["m"], self.dtype, out=b["m_low"])
-            self._proj(b["m_low"].view(B, L, M), blk["fc2"], b["o"])
-            api.add(x, b["o"].view(B, L, E), out=x)
+            api.conv_low_gelu_into(self._tokens(b["h_low"]), blk["fc1"], _ONE,
+                                   b["m_low"].permute(0, 3, 1, 2))          # GELU + rounding in the epilogue
+            self._residual(b["m_low"].view(B, L, M), blk["fc2"], x)     # x += fc2
         return x

@@ -334,6 +334,23 @@ int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stre
  * is contiguous with `input`'s dims. */
 int fb_gelu_to_low(const fb_tensor* input, fb_tensor* output, void* stream);
 
+/* Fused forms of the two chains above, for projections written as 1x1 (or
+ * any) low convolutions: the tensor-core GEMM applies them to its f32 sums in
+ * the epilogue, so the f32 intermediate never reaches memory.  Results are
+ * bit-identical to the unfused chains (the same f32 arithmetic, one rounding);
+ * layouts the tensor cores refuse compute the same chain through scratch.
+ *
+ * fb_conv_low_gelu: fb_gelu_to_low(fb_conv_low_f32(input, weight)) into a
+ * 16-bit `output` of the operands' dtype (arguments as fb_conv_low). */
+int fb_conv_low_gelu(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
+                     void* stream);
+
+/* fb_conv_low_f32_accumulate: output += fb_conv_low_f32(input, weight), the
+ * f32 `output` (conv_low_f32's output dims, any layout addressing each
+ * element once) read and written in place: a residual connection. */
+int fb_conv_low_f32_accumulate(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options,
+                               fb_tensor* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -142,3 +142,30 @@ def test_cast_to_low_strided_views(cuda, inner):
     got = api.cast_to_low(view, torch.bfloat16).float().cpu().numpy()
     exp = low(x[:, :, 1].permute(0, 2, 1, 3).numpy())
     assert np.array_equal(got, exp)
+
+
+@pytest.mark.parametrize("cout,cin,tokens", [(768, 768, 197 * 4), (128, 256, 300), (40, 24, 50)])
+def test_fused_projection_epilogues_match_the_unfused_chain(cuda, cout, cin, tokens):
+    """conv_low_gelu == gelu_to_low(conv_low_f32) and conv_low_f32_accumulate
+    == add(x, conv_low_f32), bit for bit: CTA-pair tiles (768), single-CTA
+    tiles (128) and the scratch route the tensor cores refuse (40 x 24)."""
+    g = torch.Generator(device="cpu").manual_seed(cout + cin)
+    tok = torch.randn(2, tokens, cin, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(cout, cin, 1, 1, generator=g) * cin ** -0.5).bfloat16().to(cuda)
+    xin = tok.view(2, 1, tokens, cin).permute(0, 3, 1, 2)
+    one = ConvOptions([1, 1], [1, 1], [0, 0], [0, 0])
+    ref32 = torch.empty(2, 1, tokens, cout, device=cuda)
+    api.conv_low_f32_into(xin, w, one, ref32.permute(0, 3, 1, 2))
+    # GELU + rounding in the epilogue
+    ref_low = api.gelu_to_low(ref32, torch.bfloat16)
+    got_low = torch.empty(2, 1, tokens, cout, dtype=torch.bfloat16, device=cuda)
+    api.conv_low_gelu_into(xin, w, one, got_low.permute(0, 3, 1, 2))
+    assert api.device_status() == 0
+    assert torch.equal(got_low.view(torch.int16), ref_low.view(torch.int16))
+    # residual accumulation in the epilogue
+    x0 = torch.randn(2, tokens, cout, generator=g).to(cuda)
+    want = api.add(x0, ref32.view(2, tokens, cout))
+    x = x0.clone()
+    api.conv_low_f32_accumulate(xin, w, one, x.view(2, 1, tokens, cout).permute(0, 3, 1, 2))
+    assert api.device_status() == 0
+    assert torch.equal(x, want)
