@@ -266,6 +266,19 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                             make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
                     __syncwarp();
+                    // accumulate: the chunk's eight float4 of the existing
+                    // output are loaded before any store (distinct rows, no
+                    // aliasing), so their latencies overlap
+                    float4 prev[8];
+                    if (p.accumulate) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = i * 4 + (lane >> 3), cc = lane & 7;
+                            const uint64_t rb = __shfl_sync(0xffffffffu, my_base, r);
+                            prev[i] = rb != ~0ull ? *reinterpret_cast<const float4*>(p.out + rb + c0 + 4 * cc)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int r = i * 4 + (lane >> 3), cc = lane & 7;
@@ -276,11 +289,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
                                 *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
                                     make_uint2(encode_low_pair(val.x, val.y, p.out_low),
                                                encode_low_pair(val.z, val.w, p.out_low));
-                            else if (p.accumulate) {
-                                float4* o = reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc);
-                                const float4 prev = *o;
-                                *o = make_float4(prev.x + val.x, prev.y + val.y, prev.z + val.z, prev.w + val.w);
-                            } else
+                            else if (p.accumulate)
+                                *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) =
+                                    make_float4(prev[i].x + val.x, prev[i].y + val.y, prev[i].z + val.z, prev[i].w + val.w);
+                            else
                                 *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
                         }
                     }
@@ -543,6 +555,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                             make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
                     __syncwarp();
+                    // accumulate: the chunk's eight float4 of the existing
+                    // output are loaded before any store (distinct rows, no
+                    // aliasing), so their latencies overlap
+                    float4 prev[8];
+                    if (p.accumulate) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = i * 4 + (lane >> 3), cc = lane & 7;
+                            const uint64_t rb = __shfl_sync(0xffffffffu, my_base, r);
+                            prev[i] = rb != ~0ull ? *reinterpret_cast<const float4*>(p.out + rb + c0 + 4 * cc)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int r = i * 4 + (lane >> 3), cc = lane & 7;
@@ -553,11 +578,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                 *reinterpret_cast<uint2*>(out16 + rb + c0 + 4 * cc) =
                                     make_uint2(encode_low_pair(val.x, val.y, p.out_low),
                                                encode_low_pair(val.z, val.w, p.out_low));
-                            else if (p.accumulate) {
-                                float4* o = reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc);
-                                const float4 prev = *o;
-                                *o = make_float4(prev.x + val.x, prev.y + val.y, prev.z + val.z, prev.w + val.w);
-                            } else
+                            else if (p.accumulate)
+                                *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) =
+                                    make_float4(prev[i].x + val.x, prev[i].y + val.y, prev[i].z + val.z, prev[i].w + val.w);
+                            else
                                 *reinterpret_cast<float4*>(p.out + rb + c0 + 4 * cc) = val;
                         }
                     }

@@ -99,13 +99,24 @@ __device__ __forceinline__ uint32_t encode_low_pair(float lo, float hi, uint32_t
                             : (uint32_t)encode_f16(lo) | ((uint32_t)encode_f16(hi) << 16);
 }
 
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error about
+// 2^-22; subnormal results flush to zero; -inf -> 0, NaN -> NaN).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // tanh form of GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), as
 // x / (1 + exp(-2u)): the same value without the cancellation of 1 + tanh
-// for large negative x.
+// for large negative x.  exp on the special-function unit and a fast divide
+// (relative error about 1e-5 before the 16-bit rounding that follows every
+// use; x -> -inf gives -0, x -> +inf gives x), cheap enough for a GEMM
+// epilogue to apply it at the tensor cores' pace.
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;
     const float u = k0 * fmaf(k1 * x, x * x, x);
-    return x / (1.0f + expf(-2.0f * u));
+    return __fdividef(x, 1.0f + ex2_approx(u * -2.885390081777927f));  // -2 log2(e)
 }
 
 __device__ __forceinline__ double warp_sum(double v) {
@@ -123,13 +134,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
-}
-// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error about
-// 2^-22; subnormal results flush to zero; -inf -> 0, NaN -> NaN).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
 }
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
