@@ -648,6 +648,148 @@ __global__ void __launch_bounds__(TB, CAP ? (FAM == FAM_MOMENTS ? 5 : 6) : 1) ro
     }
 }
 
+// Short rows (at most 32 x 4 x NV columns) of the exp and moments families,
+// one warp per row: the lanes read the row's float4s straight from global
+// memory (coalesced, NV in flight per lane) and reduce with shuffles only, so
+// a block holds eight rows at once and needs no barrier.  The arithmetic is
+// the streamed engine's (exp2 of the f32 difference with f32 sums for the
+// exp family; anchored f32 lane-pair moments with the same error bounds and
+// exact f64 two-pass fallback for moments and layer norm); only the order in
+// which the per-lane partials are combined differs.
+constexpr int WARP_ROWS_TB = 256;
+
+template <typename T, int NV, int FAM>
+__global__ void __launch_bounds__(WARP_ROWS_TB) rows_warp_kernel(Rows in, uint32_t op, RowOut oa, RowOut ob, ElemOut eo,
+                                                                 float eps) {
+    static_assert(FAM == FAM_EXP || FAM == FAM_MOMENTS, "exp and moments families only");
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (WARP_ROWS_TB / 32);
+    const uint64_t n = in.cols;
+    const double inv_n = 1.0 / (double)n;
+    const T* base = reinterpret_cast<const T*>(in.data) + in.offset;
+    for (uint64_t row = (uint64_t)blockIdx.x * (WARP_ROWS_TB / 32) + (threadIdx.x >> 5); row < in.rows; row += warps) {
+        const unsigned char* rp = reinterpret_cast<const unsigned char*>(base + row * in.row_stride);
+        auto valid = [&](int j) { return (lane + (uint64_t)j * 32) * 4 < n; };
+        float4 c[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) c[j] = valid(j) ? smem_load4<T>(rp, lane + (uint64_t)j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (FAM == FAM_EXP) {
+            float m = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (valid(j)) m = max3(max3(m, c[j].x, c[j].y), c[j].z, c[j].w);
+            m = warp_max(m);
+            const float2 nm2 = make_float2(-m, -m);
+            const float2 l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
+            float2 e2 = make_float2(0.0f, 0.0f);
+            const bool keep = op == STREAM_STATS + STATS_SOFTMAX;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) continue;
+                const float2 t01 = __fmul2_rn(__fadd2_rn(make_float2(c[j].x, c[j].y), nm2), l2e);
+                const float2 t23 = __fmul2_rn(__fadd2_rn(make_float2(c[j].z, c[j].w), nm2), l2e);
+                const float2 x01 = make_float2(ex2_approx(t01.x), ex2_approx(t01.y));
+                const float2 x23 = make_float2(ex2_approx(t23.x), ex2_approx(t23.y));
+                e2 = __fadd2_rn(e2, __fadd2_rn(x01, x23));
+                if (keep) c[j] = make_float4(x01.x, x01.y, x23.x, x23.y);
+            }
+            const float e = warp_sum_f(e2.x + e2.y);
+            if (op == STREAM_STATS + STATS_SOFTMAX) {
+                const float inv = __frcp_rn(e);
+                const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j)) {
+                        const float2 y01 = __fmul2_rn(make_float2(c[j].x, c[j].y), inv2);
+                        const float2 y23 = __fmul2_rn(make_float2(c[j].z, c[j].w), inv2);
+                        store_row4(eo, row, (lane + (uint64_t)j * 32) * 4, make_float4(y01.x, y01.y, y23.x, y23.y));
+                    }
+            } else if (op == STREAM_STATS + STATS_LOG_SOFTMAX) {
+                const float ls = logf(e);
+                const float2 nls = make_float2(-ls, -ls);
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j)) {
+                        const float2 y01 = __fadd2_rn(__fadd2_rn(make_float2(c[j].x, c[j].y), nm2), nls);
+                        const float2 y23 = __fadd2_rn(__fadd2_rn(make_float2(c[j].z, c[j].w), nm2), nls);
+                        store_row4(eo, row, (lane + (uint64_t)j * 32) * 4, make_float4(y01.x, y01.y, y23.x, y23.y));
+                    }
+            } else if (lane == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)((double)m + log((double)e));
+            }
+        } else {
+            // Anchored moments (bounds as in rows_stream_kernel; the f32
+            // tree over a lane's float4s has depth ceil(log2 NV), lanes and
+            // the warp combine in f64).
+            const float anc = 0.25f * ((__shfl_sync(0xffffffffu, c[0].x, 0) + __shfl_sync(0xffffffffu, c[0].y, 0)) +
+                                       (__shfl_sync(0xffffffffu, c[0].z, 0) + __shfl_sync(0xffffffffu, c[0].w, 0)));
+            const float2 na2 = make_float2(-anc, -anc);
+            float2 s2[NV], q2[NV];
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (!valid(j)) {
+                    s2[j] = q2[j] = make_float2(0.0f, 0.0f);
+                    continue;
+                }
+                const float2 d01 = __fadd2_rn(make_float2(c[j].x, c[j].y), na2);
+                const float2 d23 = __fadd2_rn(make_float2(c[j].z, c[j].w), na2);
+                s2[j] = __fadd2_rn(d01, d23);
+                q2[j] = __ffma2_rn(d01, d01, __fmul2_rn(d23, d23));
+            }
+#pragma unroll
+            for (int w = 1; w < NV; w *= 2)
+#pragma unroll
+                for (int j = 0; j + w < NV; j += 2 * w) {
+                    s2[j] = __fadd2_rn(s2[j], s2[j + w]);
+                    q2[j] = __fadd2_rn(q2[j], q2[j + w]);
+                }
+            const double D = warp_sum((double)s2[0].x + (double)s2[0].y);
+            const double Q = warp_sum((double)q2[0].x + (double)q2[0].y);
+            const double dn = (double)n;
+            double mean = (double)anc + D * inv_n;
+            double var = (Q - D * D * inv_n) * inv_n;
+            constexpr double kL = NV > 4 ? 6.0 : NV > 2 ? 5.0 : NV > 1 ? 4.0 : 3.0;  // 3 + ceil(log2 NV)
+            constexpr double kLu = kL * 5.9604644775390625e-08;
+            const double big = 1.7976931348623157e308;
+            const double A = (double)sqrtf((float)(dn * Q)) * (1.0 + 9.5367431640625e-07);
+            const bool fast = fabs(D) <= big && Q <= big && var > 1e-30 &&
+                              kLu * A * inv_n <= 9.5367431640625e-07 * fmax(fabs(mean), 1.0) && Q <= 4.0 * dn * var;
+            if (!fast) {  // warp-uniform: exact f64 two-pass
+                double e = 0.0;
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j)) e += ((double)c[j].x + (double)c[j].y) + ((double)c[j].z + (double)c[j].w);
+                mean = warp_sum(e) * inv_n;
+                double q = 0.0;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    if (!valid(j)) continue;
+                    const double e0 = (double)c[j].x - mean, e1 = (double)c[j].y - mean;
+                    const double e2 = (double)c[j].z - mean, e3 = (double)c[j].w - mean;
+                    q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+                }
+                var = warp_sum(q) * inv_n;
+            }
+            const float m32 = (float)mean;
+            const double delta = mean - (double)m32;
+            if (var < 0.0) var = 0.0;
+            if (op == STREAM_STATS + STATS_LAYER_NORM) {
+                const double inv = 1.0 / sqrt(var + (double)eps);
+                const float invf = (float)inv, dinv = (float)(delta * inv);
+                auto ln = [&](float x) { return fmaf(x - m32, invf, -dinv); };
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (valid(j))
+                        store_row4(eo, row, (lane + (uint64_t)j * 32) * 4,
+                                   make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w)));
+            } else if (lane == 0) {
+                static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
+                static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
+            }
+        }
+    }
+}
+
 // Global f32 sum into one f64: grid-stride f64 partials per block, then the
 // last block to finish folds the block partials in index order (so the
 // result does not depend on block scheduling) and re-arms the counter.
@@ -886,6 +1028,30 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
                          (in.rows <= 1 || eo.row_stride % 4 == 0)))
         return FB_ERR_UNSUPPORTED;
     const uint64_t vec = in.cols / 4;
+    // Short rows of the exp and moments families: one warp per row.
+    const bool exp_fam = op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
+                         op == STREAM_STATS + STATS_LOGSUMEXP;
+    const bool mom_fam = op == STREAM_STATS + STATS_MOMENTS || op == STREAM_STATS + STATS_LAYER_NORM;
+    if ((exp_fam || mom_fam) && vec <= 8 * 32) {
+        auto launch_w = [&](auto kernel) -> int {
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, WARP_ROWS_TB, 0) != cudaSuccess || per_sm < 1)
+                return FB_ERR_UNSUPPORTED;
+            const uint64_t want = (in.rows + WARP_ROWS_TB / 32 - 1) / (WARP_ROWS_TB / 32);
+            const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
+            kernel<<<(unsigned)(want < cap ? want : cap), WARP_ROWS_TB, 0, st>>>(in, op, a, b, eo, eps);
+            return check_launch();
+        };
+        auto by_nv = [&](auto fam_c) -> int {
+            constexpr int F = decltype(fam_c)::value;
+            if (vec <= 32) return launch_w(rows_warp_kernel<T, 1, F>);
+            if (vec <= 64) return launch_w(rows_warp_kernel<T, 2, F>);
+            if (vec <= 128) return launch_w(rows_warp_kernel<T, 4, F>);
+            if (vec <= 192) return launch_w(rows_warp_kernel<T, 6, F>);
+            return launch_w(rows_warp_kernel<T, 8, F>);
+        };
+        return exp_fam ? by_nv(std::integral_constant<int, FAM_EXP>{}) : by_nv(std::integral_constant<int, FAM_MOMENTS>{});
+    }
     // Row reductions without an elementwise output (sum, min/max, argmax,
     // mean, moments, logsumexp) run 128-thread blocks with a short ring: more
     // rows in reduction at once per SM hides each row's reduce/barrier
