@@ -1055,13 +1055,14 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
     // Row reductions without an elementwise output (sum, min/max, argmax,
     // mean, moments, logsumexp) run 128-thread blocks with a short ring: more
     // rows in reduction at once per SM hides each row's reduce/barrier
-    // latency.  Operations that also write the row (softmax, log-softmax,
-    // layer norm) measured faster with 256 threads and a deeper ring on long
-    // rows (4096 columns), and with 128 threads on short ones (768 columns,
-    // where 256 threads would leave a quarter of the block idle).
+    // latency.  Layer norm on long rows (more than 1024 columns) measured
+    // faster with 256 threads and a deeper ring.
     const bool writes_row = op == STREAM_STATS + STATS_SOFTMAX || op == STREAM_STATS + STATS_LOG_SOFTMAX ||
                             op == STREAM_STATS + STATS_LAYER_NORM;
-    const uint32_t tb = vec > 128 && vec <= (writes_row ? 256u : 8u * 128) ? 128 : 256;
+    // Since each operation family has its own registers, the exp family
+    // (softmax, log-softmax) measured faster with 128 threads on long rows
+    // too (4096 columns: 5.61 vs 5.47 TB/s); layer norm keeps 256.
+    const uint32_t tb = vec > 128 && (vec <= (writes_row ? 256u : 8u * 128) || (exp_fam && vec <= 8u * 128)) ? 128 : 256;
     const int nv = vec <= tb ? 1 : vec <= 2 * tb ? 2 : vec <= 4 * tb ? 4 : 8;
     if ((uint64_t)nv * 4 * tb < in.cols) return FB_ERR_UNSUPPORTED;
     // Ring depth: enough rows in flight to cover HBM latency, within shared memory.

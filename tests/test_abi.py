@@ -205,6 +205,25 @@ def test_validation_precedes_any_launch():
     # output aliasing a non-dense layout is rejected
     y = _desc([2, 5], _lib.F32, strides=[5, 0])
     assert lib.fb_reduce_f32(0, C.byref(x), ax, 1, 0, C.byref(y), None) == 32
+    # fused projection entry points validate like conv_low / conv_low_f32
+    xl = _desc([2, 3, 5], _lib.BF16)
+    wl = _desc([4, 3, 1], _lib.BF16)
+    y16 = _desc([2, 4, 5], _lib.BF16)
+    y32 = _desc([2, 4, 5], _lib.F32)
+    assert lib.fb_conv_low_gelu(C.byref(x), C.byref(w), C.byref(o), C.byref(y16), None) == 33  # f32 operands
+    assert lib.fb_conv_low_gelu(C.byref(xl), C.byref(wl), C.byref(o), C.byref(y32), None) == 33  # output dtype
+    assert lib.fb_conv_low_f32_accumulate(C.byref(xl), C.byref(wl), C.byref(o), C.byref(y16), None) == 33
+    assert lib.fb_conv_low_f32_accumulate(C.byref(xl), C.byref(wl), C.byref(o), C.byref(_desc([2, 4, 4], _lib.F32)),
+                                          None) == 32  # planned dims
+    # low GEMM: operands of one 16-bit dtype, planned output dims
+    ml = _desc([3, 4], _lib.BF16)
+    mr = _desc([4, 5], _lib.F16)
+    mo = _desc([3, 5], _lib.F32)
+    assert lib.fb_matmul_low_f32(C.byref(ml), C.byref(mr), C.byref(mo), None) == 32
+    mr = _desc([4, 5], _lib.BF16)
+    assert lib.fb_matmul_low_f32(C.byref(ml), C.byref(mr), C.byref(_desc([3, 4], _lib.F32)), None) == 32
+    assert lib.fb_matmul_low(C.byref(ml), C.byref(mr), C.byref(mo), None) == 33  # matmul_low writes the operands' dtype
+    assert lib.fb_matmul_low_f32(C.byref(ml), C.byref(_desc([5, 5], _lib.BF16)), C.byref(mo), None) == 15
     # status strings
     assert lib.fb_status_string(8).decode().startswith("min, max and mean")
 
