@@ -69,6 +69,14 @@ struct AttnParams {
     uint64_t o_sb, o_sh, o_sl;              // output strides (elements) of batch, head, query
     const void* mask;       // keep (u32) or additive (f32) mask, keys contiguous
     uint64_t m_sb, m_sh, m_sq;              // mask strides (elements; 0 = broadcast) of batch, head, query
+    // Key split (few query blocks over many key tiles): each CTA takes
+    // `split_tiles` key tiles of its (batch, head, query block) and leaves,
+    // per query row, a record {base, l, O[D]} in `part` (O unnormalised,
+    // base the log2 reference of its exponentials); attn_merge_kernel
+    // combines a row's records.  splits == 1: whole range, final output.
+    uint32_t splits, split_tiles;
+    uint32_t rec_rows;      // record rows per (batch, head): the query rows L
+    float* part;
 };
 
 // QT Q tiles of 128 rows per CTA: 2 (the two tiles' softmax and MMA
@@ -204,12 +212,20 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
     // Consecutive CTAs take the query blocks of one (batch, head), heaviest
     // (last, for causal) first, so the CTAs in flight share a few heads' K/V
     // in L2.
-    const uint32_t bh = blockIdx.x / p.q_blocks;
-    const uint32_t qb = p.q_blocks - 1 - blockIdx.x % p.q_blocks;
+    const uint32_t units = p.q_blocks * p.splits;
+    const uint32_t bh = blockIdx.x / units;
+    const uint32_t qb = p.q_blocks - 1 - (blockIdx.x % units) / p.splits;
+    const uint32_t split = blockIdx.x % p.splits;
+    const uint32_t j0 = split * p.split_tiles;  // first key tile of this CTA's range
     const uint32_t q0 = qb * (QT * TQ);
+    // key tiles of this CTA's range visible to each Q tile (local indices
+    // j = 0 .. n_t - 1 stand for key tiles j0 + j)
     uint32_t n_t[QT];
 #pragma unroll
-    for (int t = 0; t < QT; ++t) n_t[t] = visible_tiles(p, q0 + t * TQ);
+    for (int t = 0; t < QT; ++t) {
+        const uint32_t vis_tiles = visible_tiles(p, q0 + t * TQ);
+        n_t[t] = vis_tiles > j0 ? min(vis_tiles - j0, p.split_tiles) : 0u;
+    }
     uint32_t n_kv = 0;
 #pragma unroll
     for (int t = 0; t < QT; ++t) n_kv = max(n_kv, n_t[t]);
@@ -268,7 +284,7 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
             }
             mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
             for (int b = 0; b < C::BOXES; ++b)
-                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)(j * TK), kv_head, k_b, &k_full[s]);
+                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)((j0 + j) * TK), kv_head, k_b, &k_full[s]);
             ++issued_k;
             if (!mbar_wait(&v_empty[s], ph)) {
                 failed = true;
@@ -276,7 +292,7 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
             }
             mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
             for (int b = 0; b < C::BOXES; ++b)
-                tma_load_4d(vd + b * (TK * 128), &tmV, b * 64, (int32_t)(j * TK), kv_head, v_b, &v_full[s]);
+                tma_load_4d(vd + b * (TK * 128), &tmV, b * 64, (int32_t)((j0 + j) * TK), kv_head, v_b, &v_full[s]);
             ++issued_v;
         }
         if (failed) {
@@ -376,7 +392,7 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
             // Keys past the length or the causal edge are masked only in the
             // tiles that reach them; logits are x * sl, so the row maximum of
             // the logits is the maximum of x (sl > 0) or its minimum (sl < 0).
-            const int64_t key0 = (int64_t)j * TK;
+            const int64_t key0 = (int64_t)(j0 + j) * TK;
             const bool edge = MASK != FB_MASK_NONE || key0 + TK > (int64_t)p.Lk || key0 + TK - 1 > vis;
             if (edge || sl == 0.0f) {
                 const int64_t lim64 = min((int64_t)p.Lk - key0, vis - key0 + 1);
@@ -490,7 +506,17 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
         // depend on whether this row exists (q < L).
         const bool load = ok && n > 0;
         float* orow = p.out + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + (uint64_t)q * p.o_sl;
-        const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
+        float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
+        if (p.splits > 1) {
+            // record {base, l, O} of this row and key range (O unnormalised)
+            orow = p.part + (((uint64_t)bh * p.rec_rows + q) * p.splits + split) * (D + 2);
+            if (q < p.L) {
+                orow[0] = m_used == NEG ? 0.0f : m_used + p.shift;
+                orow[1] = load ? l : 0.0f;
+            }
+            orow += 2;
+            inv = 1.0f;
+        }
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
@@ -502,11 +528,18 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
                 for (int i = 0; i < 32; ++i) r[i] = 0u;
             }
             if (q < p.L) {
+                if (p.splits > 1) {  // records are 8-byte aligned
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4*>(orow + c * 32 + i) =
-                        make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                    __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                    for (int i = 0; i < 32; i += 2)
+                        *reinterpret_cast<float2*>(orow + c * 32 + i) =
+                            make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(orow + c * 32 + i) =
+                            make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                        __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                }
             }
         }
         tc_fence_before();
@@ -515,6 +548,42 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// Combines the key-range records of each query row: with M the largest base
+// of the ranges that saw a key, O = sum O_s 2^(base_s - M) / sum l_s
+// 2^(base_s - M) (the exponentials' common pre-scale cancels); rows with no
+// visible key are 0, as in the unsplit kernel.  One warp per row.
+template <int D>
+__global__ void attn_merge_kernel(AttnParams p) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t total = (uint64_t)p.bh * p.L;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
+    for (uint64_t w = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const uint64_t bh = w / p.L, q = w % p.L;
+        const float* rec = p.part + ((bh * p.rec_rows + q) * p.splits) * (D + 2);
+        float M = -__int_as_float(0x7f800000);
+        for (uint32_t s = 0; s < p.splits; ++s)
+            if (rec[s * (D + 2) + 1] > 0.0f) M = fmaxf(M, rec[s * (D + 2)]);
+        float L = 0.0f;
+        float o[D / 32];
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) o[i] = 0.0f;
+        for (uint32_t s = 0; s < p.splits; ++s) {
+            const float* r = rec + s * (D + 2);
+            const float l = r[1];
+            if (!(l > 0.0f)) continue;
+            const float wgt = exp2f(r[0] - M);
+            L = fmaf(l, wgt, L);
+#pragma unroll
+            for (int i = 0; i < D / 32; ++i) o[i] = fmaf(r[2 + i * 32 + lane], wgt, o[i]);
+        }
+        const uint32_t batch = (uint32_t)(bh / p.H), head = (uint32_t)(bh % p.H);
+        float* orow = p.out + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + q * p.o_sl;
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) orow[i * 32 + lane] = o[i] * inv;
     }
 }
 
@@ -645,11 +714,44 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
                                                     : attn_fwd_kernel<D, FB_MASK_NONE, QT>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return launch_status("shared-memory attribute");
-    const uint64_t grid = (uint64_t)p.q_blocks * BH;
+    uint64_t grid = (uint64_t)p.q_blocks * BH;
     if (grid == 0) return FB_OK;
+    // Fewer CTAs than one wave over long key ranges (decode of a few
+    // heads): split each CTA's key tiles so that about four waves of CTAs
+    // exist, at least two tiles per range.  A key step costs the same
+    // however few query rows are valid, so splitting pays only while SMs
+    // would otherwise idle (measured: B=8 x 32 heads x 8192 keys, 256 CTAs,
+    // is slower split).
+    p.splits = 1;
+    p.split_tiles = p.kv_tiles;
+    p.rec_rows = (uint32_t)L;  // records exist only for rows q < L
+    const uint64_t slots = (uint64_t)sm_count() * (QT == 1 ? 2 : 1);
+    if (grid < slots && p.kv_tiles >= 4) {
+        uint64_t splits = (4 * slots + grid - 1) / grid;
+        if (splits > p.kv_tiles / 2) splits = p.kv_tiles / 2;
+        const uint64_t tiles = (p.kv_tiles + splits - 1) / splits;
+        splits = (p.kv_tiles + tiles - 1) / tiles;
+        const uint64_t bytes = BH * p.rec_rows * splits * (D + 2) * sizeof(float);
+        float* part = splits > 1 ? static_cast<float*>(scratch(st, bytes, SCRATCH_ATTN_SPLIT)) : nullptr;
+        if (part) {  // none (e.g. first use inside a graph capture): whole ranges
+            p.splits = (uint32_t)splits;
+            p.split_tiles = (uint32_t)tiles;
+            p.part = part;
+            grid *= splits;
+        } else {
+            (void)cudaGetLastError();
+        }
+    }
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
     kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
     count_launch();
+    if (p.splits > 1) {
+        if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
+        const uint64_t rows = BH * L;
+        const unsigned mgrid = (unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sm_count() * 16);
+        attn_merge_kernel<D><<<mgrid, 256, 0, st>>>(p);
+        count_launch();
+    }
     return launch_status("kernel launch");
 }
 

@@ -83,3 +83,23 @@ def test_decode_row_boundary(cuda, lq):
     q, k, v = rnd((1, 8, lq, 40), 20), rnd((1, 2, 512, 40), 21), rnd((1, 2, 512, 40), 22)
     got = api.attention(*(torch.from_numpy(t).to(cuda) for t in (q, k, v)), None, AttentionOptions())
     close(got, orc.attention(q, k, v))
+
+
+@pytest.mark.parametrize("lq,lk,causal,depth", [(1, 8192, None, 128), (4, 4100, 4096, 128), (3, 2048, None, 64),
+                                                (16, 3000, 2990, 64)])
+def test_decode_tensor_core_key_split(cuda, lq, lk, causal, depth):
+    """16-bit decode on the tensor cores with the key range split across CTAs
+    (few query blocks over many key tiles) and the ranges merged on the
+    device: GQA 8 query heads over 2, causal offsets that leave the last
+    ranges partly or wholly masked; against the f64 oracle at the BF16 gate
+    and at the kernel's own accuracy."""
+    shapes = ((2, 8, lq, depth), (2, 2, lk, depth), (2, 2, lk, depth))
+    q, k, v = (low_round(rnd(s, 30 + i)) for i, s in enumerate(shapes))
+    opts = AttentionOptions(causal=causal)
+    got = api.attention_low_f32(*(torch.from_numpy(t).to(torch.bfloat16).to(cuda) for t in (q, k, v)), None, opts)
+    assert api.device_status() == 0
+    exp = orc.attention(q, k, v, causal=causal)
+    a = got.cpu().numpy().astype(np.float64)
+    err = np.abs(a - exp).max() / max(np.abs(exp).max(), 1e-30)
+    assert err <= 2e-2, err
+    assert err <= 3e-3, err  # BF16 P, f32 accumulation and merge
