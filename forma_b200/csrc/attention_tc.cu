@@ -76,6 +76,7 @@ struct AttnParams {
     // combines a row's records.  splits == 1: whole range, final output.
     uint32_t splits, split_tiles;
     uint32_t rec_rows;      // record rows per (batch, head): the query rows L
+    uint32_t q_mod;         // a row's query index is row % q_mod (GQA-packed rows; L otherwise)
     float* part;
 };
 
@@ -178,7 +179,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t q0) {
     if (q0 >= p.L) return 0;
     if (!p.causal) return p.kv_tiles;
-    const int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
+    int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
+    if (p.q_mod < p.L) last_q = min(last_q, (int64_t)p.q_mod - 1);  // packed rows: queries repeat per head
     const int64_t last_key = last_q + (int64_t)p.causal_offset;
     const int64_t need = last_key < 0 ? 0 : last_key / TK + 1;
     return (uint32_t)(need < (int64_t)p.kv_tiles ? need : p.kv_tiles);
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
         const uint32_t q = q0 + t * TQ + row;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const uint32_t n = n_t[t];
-        const int64_t vis = p.causal ? (int64_t)q + (int64_t)p.causal_offset : (int64_t)1 << 40;
+        const int64_t vis = p.causal ? (int64_t)(q % p.q_mod) + (int64_t)p.causal_offset : (int64_t)1 << 40;
         const float NEG = -__int_as_float(0x7f800000);
         const float sl = p.scale_log2;
         float m_used = NEG;  // running max (log2 units)
@@ -667,14 +669,16 @@ bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t D, 
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// L rows per head over H heads sharing Hkv key/value heads; q_mod < L when
+// a GQA group's heads are packed into the rows of one head (row % q_mod is
+// the query index).
 template <int D, int QT>
 int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLayout& kl, const RowsLayout& vl,
-             const RowsLayout& ol, const RowsLayout& ml, cudaStream_t st) {
+             const RowsLayout& ol, const RowsLayout& ml, uint64_t L, uint64_t H, uint64_t Hkv, uint64_t q_mod,
+             cudaStream_t st) {
     using C = ACfg<D, QT>;
-    const int r = (int)a.row_rank;
-    const uint64_t L = a.row_dims[r - 1], H = a.row_dims[r - 2], Lk = a.keys;
+    const uint64_t Lk = a.keys;
     const uint64_t BH = a.rows / L;
-    const uint64_t Hkv = H / a.group_size;
     CUtensorMap tq, tk, tv;
     const void* q = static_cast<const uint16_t*>(a.q) + a.q_offset;
     const void* k = static_cast<const uint16_t*>(a.k) + a.k_offset;
@@ -689,6 +693,7 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     p.H = (uint32_t)H;
     p.Hkv = (uint32_t)Hkv;
     p.q_blocks = (uint32_t)((L + QT * TQ - 1) / (QT * TQ));
+    p.q_mod = (uint32_t)q_mod;
     p.bh = (uint32_t)BH;
     p.kv_tiles = (uint32_t)((Lk + TK - 1) / TK);
     p.scale_log2 = a.scale * 1.4426950408889634f;
@@ -809,14 +814,35 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
         return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Decode of grouped heads (few query rows, no mask): the G query heads of
+    // a key/value head share its K/V, so their G x L rows become the rows of
+    // one packed head (G times fewer key steps), when each head's rows of Q
+    // and of the output are contiguous.
+    uint64_t Lp = L, Hp = H, q_mod = L;
+    const uint64_t G = a.group_size;
+    if (G > 1 && L <= 64 && a.mask_kind == FB_MASK_NONE) {
+        auto packable = [&](const RowsLayout& rl) { return L == 1 || rl.s_head == L * rl.s_row; };
+        if (packable(ql) && packable(ol)) {
+            auto pack = [&](RowsLayout& rl) {
+                if (L == 1) rl.s_row = rl.s_head;
+                rl.rows = G * L;
+                rl.heads = Hkv;
+                rl.s_head *= G;
+            };
+            pack(ql);
+            pack(ol);
+            Lp = G * L;
+            Hp = Hkv;
+        }
+    }
     // Short key ranges at D = 64 (the whole K/V loop is a few tiles, so each
     // CTA's fixed load and epilogue latency dominates): one Q tile per CTA,
     // two CTAs per SM.
     if (D == 64) {
-        return Lk <= 4 * TK ? launch_d<64, 1>(a, fmt, ql, kl, vl, ol, ml, st)
-                            : launch_d<64, 2>(a, fmt, ql, kl, vl, ol, ml, st);
+        return Lk <= 4 * TK ? launch_d<64, 1>(a, fmt, ql, kl, vl, ol, ml, Lp, Hp, Hkv, q_mod, st)
+                            : launch_d<64, 2>(a, fmt, ql, kl, vl, ol, ml, Lp, Hp, Hkv, q_mod, st);
     }
-    return launch_d<128, 2>(a, fmt, ql, kl, vl, ol, ml, st);
+    return launch_d<128, 2>(a, fmt, ql, kl, vl, ol, ml, Lp, Hp, Hkv, q_mod, st);
 }
 
 }  // namespace fb
