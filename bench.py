@@ -294,7 +294,10 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     res = {}
     fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # FMA lanes x 2 FLOP x max clock
 
-    def record(name, fn, flops, peak, peak_name, note=None):
+    def record(name, fn, flops, peak, peak_name, note=None, nbytes=None):
+        """`nbytes`: algorithmic HBM bytes per call (inputs read once, outputs
+        written once); adds the fraction of measured HBM bandwidth and which
+        roof is the nearer one."""
         for _ in range(2):
             fn()
         torch.cuda.synchronize(dev)
@@ -303,6 +306,11 @@ def run_ops(api, dev, dist, args, pk) -> dict:
         tf = flops / (ms / 1e3) / 1e12
         res[name] = {"tflops": round(dist.sum(tf), 2), "ms": round(ms, 4), "flop_per_call": flops,
                      "roofline_frac": round(tf / peak, 4), "peak_tflops": round(peak, 1), "peak": peak_name}
+        if nbytes:
+            gbs = nbytes / (ms / 1e3) / 1e9
+            res[name].update({"bytes_per_call": nbytes, "hbm_gbs": round(dist.sum(gbs), 1),
+                              "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                              "bound": "hbm" if gbs / pk["hbm_gbs"] > tf / peak else "tensor"})
         if note:
             res[name]["note"] = note
 
@@ -322,7 +330,8 @@ def run_ops(api, dev, dist, args, pk) -> dict:
         out = torch.empty(256, 256, 14, 14, device=dev)  # contiguous f32 [N, O, P, Q], as the reference allocates
         oc = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
         record(name, lambda: api.conv_low_f32_into(xv, wv, oc, out), 2 * 256 * 14 * 14 * 256 * cin * k * k,
-               pk["bf16_tflops"], "measured bf16 dense (burst)")
+               pk["bf16_tflops"], "measured bf16 dense (burst)",
+               nbytes=xn.numel() * 2 + wn.numel() * 2 + out.numel() * 4)
         del xn, wn, out
     # C4: causal attention bf16 [8, 32, 4096, 128], scale 1/sqrt(128), f32 output
     q = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
@@ -331,14 +340,25 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     L = 4096
     record("attention_bf16_causal_c4", lambda: api.attention_low_f32(q, k, v, None, AttentionOptions(causal=0)),
            4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
-           "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2")
+           "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2", nbytes=3 * q.numel() * 2 + q.numel() * 4)
+    del q, k, v
+    # decode: one query per head, 32 query heads over 8 key/value heads, 8192 keys, bf16 (HBM-bound:
+    # reads K and V once)
+    q = torch.randn(8, 32, 1, 128, device=dev, generator=g).bfloat16()
+    k = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
+    v = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
+    record("attention_bf16_decode_gqa", lambda: api.attention_low_f32(q, k, v, None, AttentionOptions()),
+           4 * 8 * 32 * 1 * 8192 * 128, pk["bf16_tflops"], "measured bf16 dense (burst)",
+           "GQA heads packed into one tile per key/value head, key range split across CTAs",
+           nbytes=2 * k.numel() * 2 + q.numel() * 2 + 8 * 32 * 128 * 4)
     del q, k, v
     # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32 output
     a = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
     b = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
     c = torch.empty(8192, 8192, device=dev)
     record("matmul_bf16_8192", lambda: api.matmul_low_f32(a, b, out=c), 2 * 8192 ** 3, pk["bf16_tflops"],
-           "measured bf16 dense (burst)", "row-major right operand (MN-major B); f32 output")
+           "measured bf16 dense (burst)", "row-major right operand (MN-major B); f32 output",
+           nbytes=a.numel() * 2 + b.numel() * 2 + c.numel() * 4)
     del a, b, c
     # C5: ViT-style encoder forward, [64,3,224,224] bf16, patch 16, 12 layers (E 768, H 12, D 64, L 197, MLP 3072)
     from forma_b200.vit import ViTConfig, ViTEncoder
