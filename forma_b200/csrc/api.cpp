@@ -354,6 +354,20 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
     // act on the f32 sums there); every other path computes an f32 result
     // (in scratch for conv_low and the epilogues) and finishes it in a
     // separate pass.
+    if (epi == CONV_EPI_ACCUMULATE) {
+        // The output is read and written while the input and weights are
+        // still being read: it may not share memory with either.
+        auto span = [](const View& v, uint64_t esz) {
+            uint64_t hi = v.offset;
+            for (size_t i = 0; i < v.dims.size(); ++i) hi += (v.dims[i] - 1) * v.strides[i];
+            const uintptr_t base = reinterpret_cast<uintptr_t>(v.data);
+            return std::make_pair(base + v.offset * esz, base + (hi + 1) * esz);
+        };
+        const auto o = span(out, 4), x = span(in, 2), k = span(w, 2);
+        auto meet = [&](std::pair<uintptr_t, uintptr_t> a) { return a.first < o.second && o.first < a.second; };
+        if (out.count > 0 && ((in.count > 0 && meet(x)) || (w.count > 0 && meet(k))))
+            return fail(FB_ERR_INVALID_INPUT, "accumulated output overlaps the convolution's input or weight");
+    }
     const bool via_scratch = round_low || epi == CONV_EPI_ACCUMULATE;
     if (via_scratch && in.count > 0 && plan.channels_per_group > 0) {
         ConvArgs d = conv_args(in, w, out, plan);

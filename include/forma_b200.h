@@ -347,7 +347,9 @@ int fb_conv_low_gelu(const fb_tensor* input, const fb_tensor* weight, const fb_c
 
 /* fb_conv_low_f32_accumulate: output += fb_conv_low_f32(input, weight), the
  * f32 `output` (conv_low_f32's output dims, any layout addressing each
- * element once) read and written in place: a residual connection. */
+ * element once) read and written in place: a residual connection.  The
+ * output may not share memory with the input or the weight
+ * (FB_ERR_INVALID_INPUT). */
 int fb_conv_low_f32_accumulate(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options,
                                fb_tensor* output, void* stream);
 

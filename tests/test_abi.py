@@ -215,6 +215,18 @@ def test_validation_precedes_any_launch():
     assert lib.fb_conv_low_f32_accumulate(C.byref(xl), C.byref(wl), C.byref(o), C.byref(y16), None) == 33
     assert lib.fb_conv_low_f32_accumulate(C.byref(xl), C.byref(wl), C.byref(o), C.byref(_desc([2, 4, 4], _lib.F32)),
                                           None) == 32  # planned dims
+    # an accumulated output may not overlap the input or the weight
+    buf = (C.c_uint16 * 4096)()
+    base = C.addressof(buf)
+    xin = _desc([1, 4, 2, 2], _lib.BF16)
+    xin.data = base
+    wk = _desc([4, 4, 1, 1], _lib.BF16)
+    wk.data = base + 1024
+    acc = _desc([1, 4, 2, 2], _lib.F32)
+    acc.data = base + 8  # inside the input's bytes
+    o1, keep1 = api._conv_options(ConvOptions([1, 1], [1, 1], [0, 0], [0, 0]))
+    assert lib.fb_conv_low_f32_accumulate(C.byref(xin), C.byref(wk), C.byref(o1), C.byref(acc), None) == 32
+    assert b"overlaps" in lib.fb_last_error()
     # low GEMM: operands of one 16-bit dtype, planned output dims
     ml = _desc([3, 4], _lib.BF16)
     mr = _desc([4, 5], _lib.F16)
