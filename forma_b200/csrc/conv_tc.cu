@@ -352,25 +352,30 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
 // arrive on the even CTA's `tempty`.
 // BN (256 or 192) is the pair tile's N: each CTA loads BN / 2 rows of B, and
 // 192 fits tile counts of N = 768 / 2304 / 3072 to 74 pairs better than 256.
-template <int BN_>
+// EPW epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter,
+// each taking half of the columns) for epilogues with per-element work (the
+// GELU), at one stage less of the ring.
+template <int BN_, int EPW = 4>
 struct PairCfg {
     static constexpr int BN = BN_;
+    static constexpr int THREADS = 64 + 32 * EPW;
     static constexpr int A_BYTES = BM * BK * 2;      // 16 KB
     static constexpr int B_BYTES = BN / 2 * BK * 2;  // 16 KB (256) / 12 KB (192)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BN == 256 ? 6 : 7;
+    static constexpr int STAGES = (BN == 256 ? 6 : 7) - (EPW == 8 ? 1 : 0);
     static constexpr int TMEM_COLS = 512;            // two BN-column accumulators
     static constexpr int EPI_PITCH = 36;
-    static constexpr int EPI_BYTES = 4 * 32 * EPI_PITCH * 4;
+    static constexpr int EPI_BYTES = EPW * 32 * EPI_PITCH * 4;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
     static_assert(SMEM <= 227 * 1024, "pair configuration exceeds shared memory");
+    static_assert(EPW == 4 || EPW == 8, "four or eight epilogue warps");
 };
 
-template <int BN_>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+template <int BN_, int EPW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN_, EPW>::THREADS, 1)
     conv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           ConvGemmParams p) {
-    using C = PairCfg<BN_>;
+    using C = PairCfg<BN_, EPW>;
     constexpr int BN = C::BN;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -398,7 +403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 2 * 4 * 32);  // both CTAs' epilogue threads
+            mbar_init(&tempty[a], 2 * EPW * 32);  // both CTAs' epilogue threads
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -518,6 +523,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // ------------------------------------------------ epilogue (both CTAs)
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
+        // columns [c_lo, c_lo + COLS) of the quarter's rows for this warp
+        constexpr int COLS = BN / (EPW / 4);
+        const int c_lo = ((warp - 2) / 4) * COLS;
         const uint32_t tempty0 = mapa_u32(smem_u32(tempty), 0);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t t = pair; t < tiles; t += pairs) {
@@ -538,10 +546,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
             const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
             if (p.c_rows) {
-                float* st = epi + quarter * (32 * C::EPI_PITCH);
+                float* st = epi + (warp - 2) * (32 * C::EPI_PITCH);
                 const uint64_t my_base = base;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = c_lo; c0 < c_lo + COLS; c0 += 32) {
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
@@ -589,7 +597,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 }
             } else {
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = c_lo; c0 < c_lo + COLS; c0 += 32) {
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
@@ -773,7 +781,7 @@ bool make_b_map(CUtensorMap* m, const BOperand& b, uint32_t box_n) {
 }
 
 // 2-CTA clusters of the pair kernel that can be resident at once (0: none).
-template <int BN>
+template <int BN, int EPW>
 int pair_clusters() {
     static int cached[64] = {0};
     int dev = 0;
@@ -782,12 +790,12 @@ int pair_clusters() {
     if (cached[dev] == 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (unsigned)sm_count());
-        cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = PairCfg<BN>::SMEM;
+        cfg.blockDim = dim3(PairCfg<BN, EPW>::THREADS);
+        cfg.dynamicSmemBytes = PairCfg<BN, EPW>::SMEM;
         int n = 0;
-        if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 PairCfg<BN>::SMEM) != cudaSuccess ||
-            cudaOccupancyMaxActiveClusters(&n, conv_gemm_pair_kernel<BN>, &cfg) != cudaSuccess || n < 1) {
+        if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN, EPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PairCfg<BN, EPW>::SMEM) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&n, conv_gemm_pair_kernel<BN, EPW>, &cfg) != cudaSuccess || n < 1) {
             (void)cudaGetLastError();
             n = -1;
         }
@@ -796,15 +804,16 @@ int pair_clusters() {
     return cached[dev] > 0 ? cached[dev] : 0;
 }
 
-template <int BN>
+template <int BN, int EPW>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, const ConvGemmParams& p, int clusters_max,
                 cudaStream_t st) {
-    if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PairCfg<BN>::SMEM) != cudaSuccess)
+    using C = PairCfg<BN, EPW>;
+    if (cudaFuncSetAttribute(conv_gemm_pair_kernel<BN, EPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
         return launch_status("shared-memory attribute");
     const uint32_t tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
     const uint32_t clusters = tiles < (uint32_t)clusters_max ? tiles : (uint32_t)clusters_max;
-    conv_gemm_pair_kernel<BN><<<2 * clusters, THREADS, PairCfg<BN>::SMEM, st>>>(ta, tb_half, p);
+    conv_gemm_pair_kernel<BN, EPW><<<2 * clusters, C::THREADS, C::SMEM, st>>>(ta, tb_half, p);
     count_launch();
     return launch_status("kernel launch");
 }
@@ -824,7 +833,8 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
         int best_clusters = 0;
         for (int bn : {256, 192}) {
             if (N % bn != 0 || (b.mn && bn != 256)) continue;
-            const int cl = bn == 256 ? pair_clusters<256>() : pair_clusters<192>();
+            const int cl = bn == 256 ? (p.act ? pair_clusters<256, 8>() : pair_clusters<256, 4>())
+                                     : (p.act ? pair_clusters<192, 8>() : pair_clusters<192, 4>());
             if (cl == 0) continue;
             const uint64_t tiles = m_pairs * (N / bn);
             const uint64_t cost = (tiles + cl - 1) / cl * bn;
@@ -838,8 +848,12 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
             CUtensorMap tb;
             if (!make_b_map(&tb, b, (uint32_t)best / 2)) return FB_ERR_UNSUPPORTED;
             p.n_tiles = (uint32_t)(N / best);
-            return best == 256 ? launch_pair<256>(ta, tb, p, best_clusters, st)
-                               : launch_pair<192>(ta, tb, p, best_clusters, st);
+            // eight epilogue warps when the epilogue applies the GELU
+            if (p.act)
+                return best == 256 ? launch_pair<256, 8>(ta, tb, p, best_clusters, st)
+                                   : launch_pair<192, 8>(ta, tb, p, best_clusters, st);
+            return best == 256 ? launch_pair<256, 4>(ta, tb, p, best_clusters, st)
+                               : launch_pair<192, 4>(ta, tb, p, best_clusters, st);
         }
     }
     const int BN = N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : N % 64 == 0 ? 64 : 0;

@@ -17,9 +17,9 @@ joined by residual additions and a GELU.  Pre-norm blocks::
 Tokens live as a channels-last [B, 1, L, E] map, so every projection is a
 1x1 convolution whose input rows are the tokens (the tensor-core implicit
 GEMM reads them in place) and whose result is written channels-last through
-a permuted output view.  The residual additions are applied to the GEMM's
-f32 sums in its epilogue (the same arithmetic as the separate add, so the
-results are identical); operands of the contractions are rounded to the low
+a permuted output view.  The residual additions and the fc1 GELU are applied
+to the GEMM's f32 sums in its epilogue (the same arithmetic as the separate
+add and GELU passes, so the results are identical); operands of the contractions are rounded to the low
 dtype at the marked points; everything else is f32.
 Weights are random (seeded); no checkpoint is involved.
 """
@@ -119,7 +119,6 @@ class ViTEncoder:
             "qkv_low": torch.empty(B, 1, L, 3 * E, dtype=low, device=dev),   # [B, L, 3, H, D] rounded once
             "a": torch.empty(B, L, E, device=dev),                          # attention output, [B, L, H, D] order
             "a_low": torch.empty(B, L, E, dtype=low, device=dev),
-            "m": torch.empty(B, 1, L, M, device=dev),
             "m_low": torch.empty(B, 1, L, M, dtype=low, device=dev),
         }
         return self._bufs
@@ -162,10 +161,9 @@ class ViTEncoder:
             self._residual(b["a_low"], blk["proj"], x)                  # x += proj (GEMM epilogue)
             # MLP sub-block
             api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])
-            # fc1 then GELU as its own pass: measured faster at these shapes
-            # than GELU in the GEMM epilogue (fb_conv_low_gelu), whose
-            # exp/divide per element nearly matches the fc1 MMA time
-            api.conv_low_f32_into(self._tokens(b["h_low"]), blk["fc1"], _ONE, b["m"].permute(0, 3, 1, 2))
-            api.gelu_to_low(b["m"], self.dtype, out=b["m_low"])
+            # fc1 with GELU and the 16-bit rounding in the GEMM epilogue
+            # (bit-identical to conv_low_f32 then gelu_to_low; the f32 fc1
+            # result never reaches HBM)
+            api.conv_low_gelu_into(self._tokens(b["h_low"]), blk["fc1"], _ONE, b["m_low"].permute(0, 3, 1, 2))
             self._residual(b["m_low"].view(B, L, M), blk["fc2"], x)     # x += fc2
         return x
