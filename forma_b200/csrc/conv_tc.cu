@@ -828,13 +828,18 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
     const uint64_t N = b.n;
     if (p.m_tiles >= 2) {
         const uint64_t m_pairs = (p.m_tiles + 1) / 2;
+        // Eight epilogue warps (two per TMEM lane quarter) for the epilogues
+        // that do more than store f32 sums: GELU, the read-modify-write add
+        // and the 16-bit rounding, each of which otherwise outlasts a short
+        // (K = 768) main loop; plain f32 stores keep four and the deeper ring.
+        const bool heavy_epilogue = p.act || p.accumulate || p.out_low;
         int best = 0;
         uint64_t best_cost = ~0ull;
         int best_clusters = 0;
         for (int bn : {256, 192}) {
             if (N % bn != 0 || (b.mn && bn != 256)) continue;
-            const int cl = bn == 256 ? (p.act ? pair_clusters<256, 8>() : pair_clusters<256, 4>())
-                                     : (p.act ? pair_clusters<192, 8>() : pair_clusters<192, 4>());
+            const int cl = bn == 256 ? (heavy_epilogue ? pair_clusters<256, 8>() : pair_clusters<256, 4>())
+                                     : (heavy_epilogue ? pair_clusters<192, 8>() : pair_clusters<192, 4>());
             if (cl == 0) continue;
             const uint64_t tiles = m_pairs * (N / bn);
             const uint64_t cost = (tiles + cl - 1) / cl * bn;
@@ -848,8 +853,7 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
             CUtensorMap tb;
             if (!make_b_map(&tb, b, (uint32_t)best / 2)) return FB_ERR_UNSUPPORTED;
             p.n_tiles = (uint32_t)(N / best);
-            // eight epilogue warps when the epilogue applies the GELU
-            if (p.act)
+            if (heavy_epilogue)
                 return best == 256 ? launch_pair<256, 8>(ta, tb, p, best_clusters, st)
                                    : launch_pair<192, 8>(ta, tb, p, best_clusters, st);
             return best == 256 ? launch_pair<256, 4>(ta, tb, p, best_clusters, st)
