@@ -99,6 +99,7 @@ SIGNATURES = {
     ),
     "fb_attention": (C.c_int, [T, T, T, C.c_uint32, T, FbAttentionOptions, T, VP]),
     "fb_attention_low_f32": (C.c_int, [T, T, T, C.c_uint32, T, FbAttentionOptions, T, VP]),
+    "fb_attention_low": (C.c_int, [T, T, T, C.c_uint32, T, FbAttentionOptions, T, VP]),
     "fb_reduce_shape": (C.c_int, [C.c_uint32, U64P, C.c_uint32, U32P, C.c_uint32, C.c_int32, C.c_int32, U64P, U32P]),
     "fb_reduce_f32": (C.c_int, [C.c_uint32, T, U32P, C.c_uint32, C.c_int32, T, VP]),
     "fb_reduce_u32": (C.c_int, [C.c_uint32, T, U32P, C.c_uint32, C.c_int32, T, VP]),

@@ -294,7 +294,8 @@ def matmul_low(left: torch.Tensor, right: torch.Tensor, out: Optional[torch.Tens
 
 # ------------------------------------------------------------- attention
 
-def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions, out=None):
+def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions, out=None,
+               out_dtype=torch.float32):
     dev = _device(query, key, value)
     kind = 0
     dm = None
@@ -303,7 +304,7 @@ def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOp
     if out is None:
         dims = attention_plan(list(query.shape), list(key.shape), list(value.shape),
                               list(mask.tensor.shape) if mask is not None else None, options)
-        out = torch.empty(dims, dtype=torch.float32, device=dev)
+        out = torch.empty(dims, dtype=out_dtype, device=dev)
     dq, dk, dv, do = describe(query), describe(key), describe(value), describe(out)
     if mask is not None:
         dm = describe(mask.tensor)
@@ -327,6 +328,17 @@ def attention_low_f32_into(query, key, value, mask: Optional[Mask], options: Att
 def attention_low_f32(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):
     """Attention from f16/bf16 operands with f32 output."""
     return _attention(lib().fb_attention_low_f32, query, key, value, mask, options)
+
+
+def attention_low_into(query, key, value, mask: Optional[Mask], options: AttentionOptions, out):
+    """attention_low into a caller-provided 16-bit output view (a dense block in any axis order)."""
+    return _attention(lib().fb_attention_low, query, key, value, mask, options, out)
+
+
+def attention_low(query, key, value, mask: Optional[Mask] = None, options: AttentionOptions = AttentionOptions()):
+    """attention_low_f32 rounded once (nearest even) to the operands' dtype
+    (tensor-core/src/low_attention.rs:38-47)."""
+    return _attention(lib().fb_attention_low, query, key, value, mask, options, out_dtype=query.dtype)
 
 
 # ------------------------------------------------------------- reductions

@@ -444,7 +444,8 @@ int conv_impl(const fb_tensor* input, const fb_tensor* weight, const fb_conv_opt
 // ------------------------------------------------------------ attention
 
 int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, uint32_t mask_kind,
-                   const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream, bool low) {
+                   const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream, bool low,
+                   bool round_low = false) {
     View qv, kv, vv, mv, out;
     FB_TRY(view_of(q, "query", &qv));
     FB_TRY(view_of(k, "key", &kv));
@@ -467,9 +468,29 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     }
     AttentionPlan plan;
     FB_TRY(attention_plan(qv.dims, kv.dims, vv.dims, mask_dims, options, &plan));
-    FB_TRY(check_output(output, "output", plan.output, FB_F32, &out));
+    FB_TRY(check_output(output, "output", plan.output, round_low ? qv.dtype : (uint32_t)FB_F32, &out));
     if (out.count == 0) return FB_OK;
-    if (plan.keys == 0) return fill_view(out, 0u, stream);
+    // attention_low (compute-cuda/src/program/builder_attention.rs:29-42):
+    // the f32 attention rounded once to the operands' 16-bit type.  The
+    // tensor-core kernel rounds in its epilogue; the other kernels compute
+    // f32 rows into scratch laid out in the output's own memory order, and
+    // a position-wise cast finishes them.
+    View res = out;
+    if (round_low) {  // check_output admits dense blocks only: scratch offsets 0..count-1
+        float* result = static_cast<float*>(scratch(stream, out.count * 4 + 256, SCRATCH_ATTN_RESULT));
+        if (!result) return fail(FB_ERR_DRIVER, "scratch allocation failed");
+        res.data = result;
+        res.offset = 0;
+        res.dtype = FB_F32;
+    }
+    auto finish = [&](int st) {
+        if (st != FB_OK || !round_low) return st;
+        Nest flat = make_nest(Dims{out.count}, Dims{1}, all_axes(1));
+        return launched(launch_cast_to_low(static_cast<const float*>(res.data), 0, flat,
+                                           static_cast<uint16_t*>(out.data) + out.offset, out.dtype, out.count, stream),
+                        "cast");
+    };
+    if (plan.keys == 0) return finish(fill_view(res, 0u, stream));
 
     // Canonical layouts (compute-cuda/src/attention_dispatch.rs:9-18): rank-2
     // operands gain a zero-stride head axis, batches broadcast with stride 0.
@@ -490,6 +511,7 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     a.k = kv.data;
     a.v = vv.data;
     a.out = static_cast<float*>(out.data);
+    a.out_low = round_low ? out.dtype : 0;
     a.dtype = qv.dtype;
     a.mask_kind = mask_kind;
     a.row_rank = (uint32_t)(r - 1);
@@ -540,9 +562,15 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     // decode shapes too); otherwise few query rows over long key ranges
     // split the keys across warps; everything else one warp per row.
     int s = low ? launch_attention_tc(a, stream) : FB_ERR_UNSUPPORTED;
-    if (s == FB_ERR_UNSUPPORTED) s = launch_attention_decode(a, stream);
+    if (s != FB_ERR_UNSUPPORTED) return launched(s, "attention");
+    if (round_low) {  // f32 rows into the scratch copy (same strides, offset 0)
+        a.out = static_cast<float*>(res.data);
+        a.out_low = 0;
+        a.o_offset = 0;
+    }
+    s = launch_attention_decode(a, stream);
     if (s == FB_ERR_UNSUPPORTED) s = launch_attention_simt(a, stream);
-    return launched(s, "attention");
+    return finish(launched(s, "attention"));
 }
 
 // MatmulPlan::new (tensor-core/src/shape.rs:148-192).
@@ -820,6 +848,11 @@ int fb_attention(const fb_tensor* query, const fb_tensor* key, const fb_tensor* 
 int fb_attention_low_f32(const fb_tensor* query, const fb_tensor* key, const fb_tensor* value, uint32_t mask_kind,
                          const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream) {
     return attention_impl(query, key, value, mask_kind, mask, options, output, stream, true);
+}
+
+int fb_attention_low(const fb_tensor* query, const fb_tensor* key, const fb_tensor* value, uint32_t mask_kind,
+                     const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream) {
+    return attention_impl(query, key, value, mask_kind, mask, options, output, stream, true, true);
 }
 
 int fb_reduce_shape(uint32_t op, const uint64_t* dims, uint32_t rank, const uint32_t* axes, uint32_t n_axes,

@@ -45,6 +45,7 @@
 #include <mutex>
 
 #include "async.cuh"
+#include "device_common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -65,7 +66,8 @@ struct AttnParams {
     float shift;            // log2 of the numerator pre-scale
     int32_t causal, causal_offset;
     uint32_t k_batch_bcast, v_batch_bcast;  // K / V shared by every batch index (stride 0)
-    float* out;             // f32 rows: depth contiguous, rows at the strides below
+    float* out;             // f32 rows (or 16-bit rows, out_low): depth contiguous, rows at the strides below
+    uint32_t out_low;       // 0: f32 output; FB_BF16 / FB_F16: each value rounded once (nearest even)
     uint64_t o_sb, o_sh, o_sl;              // output strides (elements) of batch, head, query
     const void* mask;       // keep (u32) or additive (f32) mask, keys contiguous
     uint64_t m_sb, m_sh, m_sq;              // mask strides (elements; 0 = broadcast) of batch, head, query
@@ -79,6 +81,11 @@ struct AttnParams {
     uint32_t q_mod;         // a row's query index is row % q_mod (GQA-packed rows; L otherwise)
     float* part;
 };
+
+// First element of output row (batch, head, q) when the rows are 16-bit.
+__device__ __forceinline__ uint16_t* low_row(const AttnParams& p, uint32_t batch, uint32_t head, uint32_t q) {
+    return reinterpret_cast<uint16_t*>(p.out) + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + (uint64_t)q * p.o_sl;
+}
 
 // QT Q tiles of 128 rows per CTA: 2 (the two tiles' softmax and MMA
 // ping-pong on one SM) or 1 (short key ranges at D = 64: 256 TMEM columns and
@@ -535,6 +542,15 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
                     for (int i = 0; i < 32; i += 2)
                         *reinterpret_cast<float2*>(orow + c * 32 + i) =
                             make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+                } else if (p.out_low) {  // 16-bit rows, 16-byte aligned (host)
+                    uint4* dst = reinterpret_cast<uint4*>(low_row(p, batch, head, q) + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8)
+                        dst[i / 8] = make_uint4(
+                            encode_low_pair(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[i + 4]) * inv, __uint_as_float(r[i + 5]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[i + 6]) * inv, __uint_as_float(r[i + 7]) * inv, p.out_low));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
@@ -582,10 +598,17 @@ __global__ void attn_merge_kernel(AttnParams p) {
             for (int i = 0; i < D / 32; ++i) o[i] = fmaf(r[2 + i * 32 + lane], wgt, o[i]);
         }
         const uint32_t batch = (uint32_t)(bh / p.H), head = (uint32_t)(bh % p.H);
-        float* orow = p.out + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + q * p.o_sl;
         const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        if (p.out_low) {
+            uint16_t* lrow = low_row(p, batch, head, (uint32_t)q);
 #pragma unroll
-        for (int i = 0; i < D / 32; ++i) orow[i * 32 + lane] = o[i] * inv;
+            for (int i = 0; i < D / 32; ++i)
+                lrow[i * 32 + lane] = p.out_low == FB_BF16 ? encode_bf16(o[i] * inv) : encode_f16(o[i] * inv);
+        } else {
+            float* orow = p.out + (uint64_t)batch * p.o_sb + (uint64_t)head * p.o_sh + q * p.o_sl;
+#pragma unroll
+            for (int i = 0; i < D / 32; ++i) orow[i * 32 + lane] = o[i] * inv;
+        }
     }
 }
 
@@ -706,7 +729,8 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     p.causal_offset = a.causal_offset;
     p.k_batch_bcast = kl.batch_bcast ? 1 : 0;
     p.v_batch_bcast = vl.batch_bcast ? 1 : 0;
-    p.out = a.out + a.o_offset;
+    p.out = a.out_low ? reinterpret_cast<float*>(reinterpret_cast<uint16_t*>(a.out) + a.o_offset) : a.out + a.o_offset;
+    p.out_low = a.out_low;
     p.o_sb = ol.s_batch;
     p.o_sh = ol.s_head;
     p.o_sl = ol.s_row;
@@ -792,9 +816,10 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
     if (ql.batch_bcast || ol.batch_bcast) return FB_ERR_UNSUPPORTED;  // distinct query rows per batch index
     if (ql.batch * H * L != a.rows || ol.batch != ql.batch) return FB_ERR_UNSUPPORTED;
     if ((!kl.batch_bcast && kl.batch != ql.batch) || (!vl.batch_bcast && vl.batch != ql.batch)) return FB_ERR_UNSUPPORTED;
-    // f32 output rows take float4 stores: 16-byte aligned rows
-    auto mult4 = [](uint64_t s, uint64_t n) { return n <= 1 || s % 4 == 0; };
-    if (!mult4(ol.s_row, L) || !mult4(ol.s_head, H) || !mult4(ol.s_batch, ol.batch)) return FB_ERR_UNSUPPORTED;
+    // output rows take 16-byte stores (float4, or eight 16-bit values): 16-byte aligned rows
+    const uint64_t o_vec = a.out_low ? 8 : 4;
+    auto mult = [o_vec](uint64_t s, uint64_t n) { return n <= 1 || s % o_vec == 0; };
+    if (!mult(ol.s_row, L) || !mult(ol.s_head, H) || !mult(ol.s_batch, ol.batch)) return FB_ERR_UNSUPPORTED;
     // Masks (32-bit elements) are read 16 bytes at a time along contiguous
     // keys; rows start 16-byte aligned.  Broadcast axes have stride 0.
     RowsLayout ml;
@@ -810,7 +835,7 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
         return (reinterpret_cast<uintptr_t>(p) + off * esz) % 16 == 0;
     };
     if (!aligned(a.q, a.q_offset, 2) || !aligned(a.k, a.k_offset, 2) || !aligned(a.v, a.v_offset, 2) ||
-        !aligned(a.out, a.o_offset, 4))
+        !aligned(a.out, a.o_offset, a.out_low ? 2 : 4))
         return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);

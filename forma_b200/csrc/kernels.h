@@ -81,7 +81,8 @@ enum ScratchSlot : int {
     SCRATCH_CONV_PATCH = 3,   // non-overlapping patches gathered into [N*P*Q, C*kh*kw]
     SCRATCH_STATS = 4,        // f32 statistics result before low rounding
     SCRATCH_ATTN_SPLIT = 5,   // split-key attention partials (f64 per row and key range)
-    SCRATCH_SLOTS = 6,
+    SCRATCH_ATTN_RESULT = 6,  // f32 attention result before low rounding
+    SCRATCH_SLOTS = 7,
 };
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
@@ -182,7 +183,8 @@ struct AttnArgs {
     const void* k = nullptr;
     const void* v = nullptr;
     const void* mask = nullptr;
-    float* out = nullptr;
+    float* out = nullptr;   // f32 rows, or 16-bit rows (o_offset in 2-byte elements) when out_low != 0
+    uint32_t out_low = 0;   // 0, or FB_BF16 / FB_F16: rows rounded once (nearest even); tensor-core path only
     uint32_t dtype = FB_F32;
     uint32_t mask_kind = FB_MASK_NONE;
     // Row nest over [batch..., heads, queries] with per-operand strides; K/V

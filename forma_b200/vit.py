@@ -9,7 +9,8 @@ joined by residual additions and a GELU.  Pre-norm blocks::
     for each layer:
         h  = LN(x)                                     layer_norm, eps 1e-5, rounded to BF16 as stored
         q, k, v = heads(h W_qkv)                       1x1 conv rounded to BF16 in its epilogue
-        x  = x + concat_heads(attention(q, k, v)) W_o  fused attention, 1x1 conv adding into x
+        x  = x + concat_heads(attention(q, k, v)) W_o  fused attention rounded to BF16 in its epilogue,
+                                                       1x1 conv adding into x
         h  = LN(x)
         x  = x + GELU(h W_1) W_2                        1x1 convs, GELU rounded to BF16, the second
                                                        conv adding into x
@@ -19,8 +20,9 @@ Tokens live as a channels-last [B, 1, L, E] map, so every projection is a
 GEMM reads them in place) and whose result is written channels-last through
 a permuted output view.  The residual additions and the fc1 GELU are applied
 to the GEMM's f32 sums in its epilogue (the same arithmetic as the separate
-add and GELU passes, so the results are identical); operands of the contractions are rounded to the low
-dtype at the marked points; everything else is f32.
+add and GELU passes, so the results are identical); operands of the
+contractions are rounded to the low dtype at the marked points; everything
+else is f32.
 Weights are random (seeded); no checkpoint is involved.
 """
 
@@ -117,8 +119,7 @@ class ViTEncoder:
             "patches": torch.empty(B, G, G, E, device=dev),      # channels-last conv result
             "h_low": torch.empty(B, L, E, dtype=low, device=dev),
             "qkv_low": torch.empty(B, 1, L, 3 * E, dtype=low, device=dev),   # [B, L, 3, H, D] rounded once
-            "a": torch.empty(B, L, E, device=dev),                          # attention output, [B, L, H, D] order
-            "a_low": torch.empty(B, L, E, dtype=low, device=dev),
+            "a_low": torch.empty(B, L, E, dtype=low, device=dev),            # attention output, [B, L, H, D] order
             "m_low": torch.empty(B, 1, L, M, dtype=low, device=dev),
         }
         return self._bufs
@@ -156,8 +157,8 @@ class ViTEncoder:
             api.conv_low_into(self._tokens(b["h_low"]), blk["qkv"], _ONE, b["qkv_low"].permute(0, 3, 1, 2))
             qkv = b["qkv_low"].view(B, L, 3, H, D)
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))   # [B, H, L, D] views
-            api.attention_low_f32_into(q, k, v, None, opts, b["a"].view(B, L, H, D).permute(0, 2, 1, 3))
-            api.cast_to_low_into(b["a"], b["a_low"])
+            # attention rounded to the low dtype in its epilogue (attention_low)
+            api.attention_low_into(q, k, v, None, opts, b["a_low"].view(B, L, H, D).permute(0, 2, 1, 3))
             self._residual(b["a_low"], blk["proj"], x)                  # x += proj (GEMM epilogue)
             # MLP sub-block
             api.layer_norm_low(x, [2], cfg.eps, self.dtype, out=b["h_low"])

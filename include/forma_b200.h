@@ -189,14 +189,27 @@ int fb_attention(const fb_tensor* query, const fb_tensor* key,
                  fb_tensor* output, void* stream);
 
 /* TensorLowAttentionBackend::attention_low_f32 (tensor-core/src/
- * low_attention.rs:28-49; replaces compute-cuda/src/low_attention.rs:4-28).
- * F16/BF16 Q/K/V of one dtype, f32 output.  Dense [..., L, D] heads with
- * D in {64, 128} and no mask tensor run as a fused tcgen05 flash kernel;
- * other geometries run a CUDA-core online-softmax kernel. */
+ * low_attention.rs:28-37; replaces compute-cuda/src/low_attention.rs:4-28).
+ * F16/BF16 Q/K/V of one dtype, f32 output.  Heads with unit-stride depth
+ * D in {64, 128} and 16-byte aligned rows (keep or additive masks included)
+ * run as a fused tcgen05 flash kernel; other geometries run CUDA-core
+ * online-softmax kernels. */
 int fb_attention_low_f32(const fb_tensor* query, const fb_tensor* key,
                          const fb_tensor* value, uint32_t mask_kind,
                          const fb_tensor* mask, fb_attention_options options,
                          fb_tensor* output, void* stream);
+
+/* TensorLowAttentionBackend::attention_low (tensor-core/src/
+ * low_attention.rs:38-47; the CUDA program builder's attention_low,
+ * compute-cuda/src/program/builder_attention.rs:29-42): attention_low_f32
+ * rounded once, nearest-even, into the operands' 16-bit dtype, which the
+ * output must have.  On the tcgen05 path the rounding happens in the
+ * kernel's epilogue (no f32 result in memory); otherwise an f32 result in
+ * library scratch is cast afterwards. */
+int fb_attention_low(const fb_tensor* query, const fb_tensor* key,
+                     const fb_tensor* value, uint32_t mask_kind,
+                     const fb_tensor* mask, fb_attention_options options,
+                     fb_tensor* output, void* stream);
 
 /* -------------------------------------------------------------- reduction */
 

@@ -236,6 +236,19 @@ def test_validation_precedes_any_launch():
     assert lib.fb_matmul_low_f32(C.byref(ml), C.byref(mr), C.byref(_desc([3, 4], _lib.F32)), None) == 32
     assert lib.fb_matmul_low(C.byref(ml), C.byref(mr), C.byref(mo), None) == 33  # matmul_low writes the operands' dtype
     assert lib.fb_matmul_low_f32(C.byref(ml), C.byref(_desc([5, 5], _lib.BF16)), C.byref(mo), None) == 15
+    # attention_low: one 16-bit operand dtype, output in that dtype, a dense output block
+    ao = api._attn_options(AttentionOptions())
+    aq, ak = _desc([2, 3, 4], _lib.BF16), _desc([2, 7, 4], _lib.BF16)
+    a16 = _desc([2, 3, 4], _lib.BF16)
+    args = lambda q, k, v, out: (C.byref(q), C.byref(k), C.byref(v), 0, None, ao, C.byref(out), None)
+    af = _desc([2, 3, 4], _lib.F32)
+    assert lib.fb_attention_low(*args(af, af, af, a16)) == 33  # f32 operands
+    assert lib.fb_attention_low(*args(aq, _desc([2, 7, 4], _lib.F16), ak, a16)) == 13
+    assert lib.fb_attention_low(*args(aq, ak, ak, _desc([2, 3, 4], _lib.F32))) == 33  # output dtype
+    assert lib.fb_attention_low(*args(aq, ak, ak, _desc([2, 3, 4], _lib.F16))) == 33
+    gap = _desc([2, 3, 4], _lib.BF16, strides=[16, 5, 1], storage=32)  # rows with gaps: not a dense block
+    assert lib.fb_attention_low(*args(aq, ak, ak, gap)) == 32
+    assert b"address each element once" in lib.fb_last_error()
     # status strings
     assert lib.fb_status_string(8).decode().startswith("min, max and mean")
 
