@@ -1018,9 +1018,29 @@ int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stre
                        reinterpret_cast<uintptr_t>(xa + x.offset) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(ya + y.offset) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(o + out.offset) % 16 == 0;
-    Nest xn = make_nest(x.dims, x.strides, all_axes(x.dims.size()));
-    Nest yn = make_nest(y.dims, y.strides, all_axes(y.dims.size()));
-    Nest on = make_nest(out.dims, out.strides, all_axes(out.dims.size()));
+    // One nest over the output's dims for all three views: unit axes
+    // dropped, adjacent axes merged only where every view allows it, so the
+    // kernel decomposes each index once for all three.
+    Nest xn, yn, on;
+    for (size_t i = 0; i < out.dims.size(); ++i) {
+        if (out.dims[i] == 1) continue;
+        const uint32_t r = on.rank;
+        auto merges = [&](const Nest& n, uint64_t stride) { return n.strides[r - 1] == stride * out.dims[i]; };
+        if (r > 0 && merges(xn, x.strides[i]) && merges(yn, y.strides[i]) && merges(on, out.strides[i])) {
+            for (Nest* n : {&xn, &yn, &on}) n->dims[r - 1] *= out.dims[i];
+            xn.strides[r - 1] = x.strides[i];
+            yn.strides[r - 1] = y.strides[i];
+            on.strides[r - 1] = out.strides[i];
+        } else {
+            for (Nest* n : {&xn, &yn, &on}) {
+                n->dims[r] = out.dims[i];
+                n->rank = r + 1;
+            }
+            xn.strides[r] = x.strides[i];
+            yn.strides[r] = y.strides[i];
+            on.strides[r] = out.strides[i];
+        }
+    }
     return launched(launch_add(xa, x.offset, xn, ya, y.offset, yn, o, out.offset, on, out.count, dense, stream), "add");
 }
 

@@ -754,6 +754,23 @@ __global__ void patches_kernel(const E* x, uint64_t off, uint64_t sn, uint64_t s
     }
 }
 
+// The same gather eight elements (16 bytes) at a time, for windows whose
+// width S is a multiple of eight over a unit-stride width axis with all other
+// strides (and the offset) multiples of eight elements, in 32-bit index
+// arithmetic: one index decomposition per 16-byte load and store.
+__global__ void patches_vec8_kernel(const uint16_t* x, uint64_t off, uint64_t sn, uint64_t sc, uint64_t sh, uint32_t Cc,
+                                    uint32_t R, uint32_t S, uint32_t P, uint32_t Q, uint32_t runs, uint16_t* out) {
+    const uint32_t K = Cc * R * S;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < runs; t += gridDim.x * blockDim.x) {
+        const uint32_t i = t * 8;
+        const uint32_t m = i / K, k = i % K;
+        const uint32_t s = k % S, r = (k / S) % R, c = k / (S * R);
+        const uint32_t q = m % Q, pp = (m / Q) % P, n = m / (Q * P);
+        const uint64_t src = off + n * sn + c * sc + ((uint64_t)pp * R + r) * sh + (uint64_t)q * S + s;
+        reinterpret_cast<uint4*>(out)[t] = *reinterpret_cast<const uint4*>(x + src);
+    }
+}
+
 template <int BN>
 int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams& p, cudaStream_t st) {
     using C = Cfg<BN>;
@@ -966,11 +983,23 @@ int launch_patches(const ConvArgs& a, void* stream) {
     if (!pa) return FB_ERR_DRIVER;
     {
         const uint64_t total = M * K;
-        const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
-        patches_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.input), a.in_offset, a.in_stride_n,
-                                                        a.in_stride_c, a.in_strides[0], a.in_strides[1], (uint32_t)C,
-                                                        (uint32_t)R, (uint32_t)S, (uint32_t)P, (uint32_t)Q, M,
-                                                        static_cast<uint16_t*>(pa));
+        const bool vec8 = S % 8 == 0 && a.in_strides[1] == 1 && a.in_offset % 8 == 0 && a.in_stride_n % 8 == 0 &&
+                          a.in_stride_c % 8 == 0 && a.in_strides[0] % 8 == 0 && total < (1ull << 32) &&
+                          reinterpret_cast<uintptr_t>(a.input) % 16 == 0 && reinterpret_cast<uintptr_t>(pa) % 16 == 0;
+        if (vec8) {
+            const uint64_t runs = total / 8;
+            const unsigned grid = (unsigned)std::min<uint64_t>((runs + 255) / 256, (uint64_t)sm_count() * 16);
+            patches_vec8_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.input), a.in_offset, a.in_stride_n,
+                                                      a.in_stride_c, a.in_strides[0], (uint32_t)C, (uint32_t)R,
+                                                      (uint32_t)S, (uint32_t)P, (uint32_t)Q, (uint32_t)runs,
+                                                      static_cast<uint16_t*>(pa));
+        } else {
+            const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
+            patches_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(a.input), a.in_offset,
+                                                            a.in_stride_n, a.in_stride_c, a.in_strides[0],
+                                                            a.in_strides[1], (uint32_t)C, (uint32_t)R, (uint32_t)S,
+                                                            (uint32_t)P, (uint32_t)Q, M, static_cast<uint16_t*>(pa));
+        }
         count_launch();
         if (cudaGetLastError() != cudaSuccess) return launch_status("patch gather");
     }

@@ -29,6 +29,32 @@ __global__ void add_kernel(const float* a, uint64_t a_off, Nest an, const float*
         out[out_off + nest_offset(on, i)] = __fadd_rn(a[a_off + nest_offset(an, i)], b[b_off + nest_offset(bn, i)]);
 }
 
+// Every view has the output's dims (broadcast axes with stride 0) and a
+// contiguous innermost axis whose length is a multiple of four, each run
+// 16-byte aligned: one decomposition of the index per four elements serves
+// all three views (in 32-bit arithmetic when the element count allows).
+template <typename I>
+__global__ void add_vec4_kernel(const float* a, Nest an, const float* b, Nest bn, float* out, Nest on, I count4) {
+    for (I t = (I)blockIdx.x * blockDim.x + threadIdx.x; t < count4; t += (I)gridDim.x * blockDim.x) {
+        I lin = t * 4;
+        uint64_t oa = 0, ob = 0, oo = 0;
+#pragma unroll
+        for (int d = FB_MAX_RANK - 1; d >= 0; --d) {
+            if (d < (int)on.rank) {
+                const I dim = (I)on.dims[d];
+                const uint64_t c = lin % dim;
+                lin /= dim;
+                oa += c * an.strides[d];
+                ob += c * bn.strides[d];
+                oo += c * on.strides[d];
+            }
+        }
+        const float4 x = *reinterpret_cast<const float4*>(a + oa), y = *reinterpret_cast<const float4*>(b + ob);
+        *reinterpret_cast<float4*>(out + oo) =
+            make_float4(__fadd_rn(x.x, y.x), __fadd_rn(x.y, y.y), __fadd_rn(x.z, y.z), __fadd_rn(x.w, y.w));
+    }
+}
+
 // Both operands dense and the same shape: four elements per thread.
 __global__ void add_dense_kernel(const float4* a, const float4* b, float4* out, uint64_t count4) {
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count4; i += (uint64_t)gridDim.x * blockDim.x) {
@@ -68,6 +94,20 @@ unsigned grid_of(uint64_t work) {
 
 }  // namespace
 
+bool add_vec4_ok(const float* a, const Nest& an, const float* b, const Nest& bn, const float* out, const Nest& on) {
+    const uint32_t r = on.rank;
+    if (r == 0 || an.rank != r || bn.rank != r || on.dims[r - 1] % 4 != 0) return false;
+    for (const Nest* n : {&an, &bn, &on}) {
+        if (n->strides[r - 1] != 1) return false;
+        for (uint32_t d = 0; d < r; ++d) {
+            if (n->dims[d] != on.dims[d]) return false;
+            if (d + 1 < r && n->strides[d] % 4 != 0) return false;
+        }
+    }
+    auto al = [](const float* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+    return al(a) && al(b) && al(out);
+}
+
 int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, uint64_t b_off, const Nest& bn, float* out,
                uint64_t out_off, const Nest& on, uint64_t count, bool dense, void* stream) {
     if (count == 0) return FB_OK;
@@ -76,6 +116,13 @@ int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, u
         add_dense_kernel<<<grid_of(count / 4), BLOCK, 0, st>>>(reinterpret_cast<const float4*>(a + a_off),
                                                               reinterpret_cast<const float4*>(b + b_off),
                                                               reinterpret_cast<float4*>(out + out_off), count / 4);
+    } else if (add_vec4_ok(a + a_off, an, b + b_off, bn, out + out_off, on)) {
+        if (count < (1ull << 32))
+            add_vec4_kernel<uint32_t><<<grid_of(count / 4), BLOCK, 0, st>>>(a + a_off, an, b + b_off, bn, out + out_off, on,
+                                                                           (uint32_t)(count / 4));
+        else
+            add_vec4_kernel<uint64_t><<<grid_of(count / 4), BLOCK, 0, st>>>(a + a_off, an, b + b_off, bn, out + out_off, on,
+                                                                           count / 4);
     } else {
         add_kernel<<<grid_of(count), BLOCK, 0, st>>>(a, a_off, an, b, b_off, bn, out, out_off, on, count);
     }

@@ -96,6 +96,10 @@ def test_patch_convolution_route(cuda, contiguous_weights):
     assert err <= 2e-2, err
     # f32 accumulation of exactly representable products: far tighter than the gate
     assert err <= 1e-4, err
+    # channels-last storage (width stride 3): the element-wise gather, same GEMM, same bits
+    xl = x.to(cuda).permute(0, 2, 3, 1).contiguous().permute(0, 3, 1, 2)
+    out_l = api.conv_low_f32(xl, wd, ConvOptions([16, 16], [1, 1], [0, 0], [0, 0])).cpu().numpy()
+    assert np.array_equal(out_l.view(np.uint32), out.view(np.uint32))
 
 
 def test_add_broadcast_and_strided_output(cuda):
@@ -114,6 +118,22 @@ def test_add_broadcast_and_strided_output(cuda):
     assert np.array_equal(x.cpu().numpy(), (a.numpy() * 2).astype(np.float32))
     with pytest.raises(api.TensorError):
         api.add(big[:, :5], big[:, 1:], out=big[:, 1:])  # overlapping, not identical
+
+
+@pytest.mark.parametrize("inner", [16, 768])
+def test_add_four_wide_runs_over_strided_views(cuda, inner):
+    """Views whose innermost axis is contiguous (a multiple of four): the
+    encoder's [cls; patches] + pos (offset output rows, a batch-broadcast
+    operand) and a permuted operand; one f32 add, bit-exact."""
+    g = torch.Generator(device="cpu").manual_seed(inner)
+    a = torch.randn(9, 4, inner, generator=g)
+    pos = torch.randn(1, 10, inner, generator=g)
+    big = torch.zeros(4, 10, inner, device=cuda)
+    api.add(a.to(cuda).permute(1, 0, 2), pos.to(cuda)[:, 1:].expand(4, 9, inner), out=big[:, 1:])
+    got = big.cpu().numpy()
+    exp = (a.permute(1, 0, 2).numpy() + pos[:, 1:].numpy()).astype(np.float32)
+    assert np.array_equal(got[:, 1:].view(np.uint32), exp.view(np.uint32))
+    assert (got[:, 0] == 0).all()
 
 
 def test_gelu_to_low_matches_tanh_form(cuda):
