@@ -633,6 +633,19 @@ def run_profile(args) -> int:
             api.reduce_f32(ReduceOp.Max, x, [1])
             api.argmax(x, 1)
             api.moments(x, [1])
+    elif name in ("c5_qkv", "c5_fc1"):
+        # one C5 layer projection as a 1x1 convolution on channels-last tokens:
+        # QKV [64*197, 768] x [768, 2304] rounded to BF16, or fc1 (x 3072) with GELU
+        cout = 2304 if name == "c5_qkv" else 3072
+        t = torch.randn(64, 197, 768, device=dev, generator=g).bfloat16()
+        w = (torch.randn(cout, 768, 1, 1, device=dev, generator=g) * 768 ** -0.5).bfloat16()
+        o = torch.empty(64, 1, 197, cout, dtype=torch.bfloat16, device=dev)
+        xin, ov = t.view(64, 1, 197, 768).permute(0, 3, 1, 2), o.permute(0, 3, 1, 2)
+        one = ConvOptions([1, 1], [1, 1], [0, 0], [0, 0])
+        if name == "c5_qkv":
+            fn = lambda: api.conv_low_into(xin, w, one, ov)  # noqa: E731
+        else:
+            fn = lambda: api.conv_low_gelu_into(xin, w, one, ov)  # noqa: E731
     elif name == "vit_c5":
         from forma_b200.vit import ViTConfig, ViTEncoder
 
@@ -664,6 +677,7 @@ def main(argv=None) -> int:
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--profile", default=None,
                     help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, vit_c5, "
+                         "c5_qkv, c5_fc1, "
                          "rows_max_argmax_moments, "
                          "conv_c1, rows_softmax, rows_argmax, rows_moments)")
     args = ap.parse_args(argv)

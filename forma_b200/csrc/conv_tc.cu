@@ -545,7 +545,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN_, EPW>::T
             }
             uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
             const uint32_t taddr = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
-            if (p.c_rows) {
+            if (p.c_rows && p.out_low) {
+                // 16-bit rows straight from registers: each lane writes its
+                // own row's 32 columns (64 bytes) as four 16-byte stores, or
+                // eight 8-byte ones where the row is only 8-byte aligned.
+                // (Staging through shared memory for row-coalesced stores
+                // measured slower here: the stores queued behind the ring's
+                // TMA and tensor-core traffic.)
+#pragma unroll 1
+                for (int c0 = c_lo; c0 < c_lo + COLS; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    tmem_wait_ld();
+                    if (p.act) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_tanh(__uint_as_float(v[j])));
+                    }
+                    if (base != ~0ull) {
+                        uint32_t w[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            w[j] = encode_low_pair(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]), p.out_low);
+                        uint16_t* dst = out16 + base + c0;
+                        if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) reinterpret_cast<uint2*>(dst)[q] = make_uint2(w[2 * q], w[2 * q + 1]);
+                        }
+                    }
+                }
+            } else if (p.c_rows) {
                 float* st = epi + (warp - 2) * (32 * C::EPI_PITCH);
                 const uint64_t my_base = base;
 #pragma unroll 1

@@ -101,3 +101,22 @@ def test_matmul_many_tiles(cuda, M, K, N):
         again = api.matmul_low_f32(a, b)
         assert torch.equal(again, first)
     assert api.device_status() == 0
+
+
+@pytest.mark.parametrize("offset", [0, 4])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_matmul_low_into_offset_output(cuda, dtype, offset):
+    """matmul_low into a dense output starting `offset` elements into its
+    buffer: at 4 every row is 8- but not 16-byte aligned, so the CTA-pair
+    epilogue takes its 8-byte row stores; the bits equal the fresh result
+    and the elements around the view stay untouched."""
+    g = torch.Generator(device="cpu").manual_seed(17)
+    a = torch.randn(512, 256, generator=g).to(dtype).to(cuda)
+    b = torch.randn(256, 768, generator=g).to(dtype).to(cuda)
+    want = api.matmul_low(a, b)
+    flat = torch.full((512 * 768 + 16,), 7.0, dtype=dtype, device=cuda)
+    out = flat[offset:offset + 512 * 768].view(512, 768)
+    api.matmul_low(a, b, out=out)
+    assert api.device_status() == 0
+    assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+    assert bool((flat[:offset] == 7.0).all()) and bool((flat[offset + 512 * 768:] == 7.0).all())
