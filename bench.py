@@ -8,10 +8,11 @@ layer-norm statistics (moments) and a global sum over all ranks' rows (one
 summed over all ranks (weak scaling: each rank owns 65536 rows).  X is 1.07 GB
 per pass, larger than the 126 MB L2, so no flush is needed between passes.
 
-The JSON line also reports, per convolution / attention workload, TFLOP/s
-against the roofline (key "ops"), the dominant kernel's roofline, the CPU
-baseline (the oracle on the host's cores) and an end-to-end number through
-host buffers.
+The JSON line also reports, per convolution / attention / GEMM / encoder
+workload at its fixed size (sharded across the ranks: strong scaling),
+TFLOP/s against the roofline (key "ops"), the dominant kernel's roofline, the
+CPU baseline (the oracle on the host's cores, rows and one unit of each op
+workload) and an end-to-end number through host buffers.
 
 ``--impl reference`` times the reference's CPU path (the oracle port of its
 f64 algorithms, all host threads) on a bounded sample of the same workload.
@@ -175,6 +176,7 @@ class Dist:
     def init(self):
         torch = self.torch
         torch.cuda.set_device(self.local)
+        self.comm = None
         if self.world > 1:
             from datetime import timedelta
 
@@ -182,6 +184,17 @@ class Dist:
             torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=60),
                                                  device_id=torch.device("cuda", self.local))
             self.pg = torch.distributed.group.WORLD
+            # The global sum's all-reduce runs inside the backend, on an NCCL
+            # communicator made through its C ABI: rank 0 creates the id and
+            # the process group only carries it to the other ranks.
+            from forma_b200.api import NcclCommunicator
+
+            dev = torch.device("cuda", self.local)
+            uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+            if self.rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(NcclCommunicator.unique_id()), dtype=torch.uint8))
+            torch.distributed.broadcast(uid, 0)
+            self.comm = NcclCommunicator.init_rank(self.world, bytes(uid.cpu().numpy().tobytes()), self.rank, dev)
 
     def barrier(self):
         if self.world > 1:
@@ -202,6 +215,10 @@ class Dist:
         return float(t.item())
 
     def close(self):
+        if self.comm is not None:
+            self.torch.cuda.synchronize()
+            self.comm.destroy()
+            self.comm = None
         if self.world > 1:
             self.torch.distributed.destroy_process_group()
 
@@ -226,7 +243,7 @@ def row_ops(api, x, dist, timers=None):
     run("row_argmax", lambda: api.argmax(x, 1))
     run("softmax", lambda: api.softmax(x, [1]))
     run("moments", lambda: api.moments(x, [1]))
-    run("global_sum", lambda: api.global_sum(x, dist.pg))
+    run("global_sum", lambda: api.global_sum(x, dist.comm))
     return out
 
 
@@ -258,8 +275,9 @@ def cpu_baseline_rows(sample_rows: int, repeats: int = 1) -> dict:
     dt = (time.perf_counter() - t0) / repeats
     b = sum(row_bytes(sample_rows, COLS).values())
     return {"value": b / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{sample_rows} rows x {COLS} f32 through sum, max, argmax, softmax, moments, global sum "
-                      f"(oracle, f64 arithmetic, {threads} threads), {dt:.2f} s per pass"}
+            "sample": f"{sample_rows} of {ROWS} rows x {COLS} f32 through sum, max, argmax, softmax, moments, "
+                      f"global sum (oracle, f64 arithmetic, {threads} threads), {dt:.2f} s per pass; GB/s "
+                      f"extrapolated per byte to the whole workload"}
 
 
 # ------------------------------------------------- conv / attention workloads
@@ -281,11 +299,15 @@ def time_op(torch, fn, iters, flush_buf, stream):
 
 
 def run_ops(api, dev, dist, args, pk) -> dict:
-    """Per-workload TFLOP/s of the convolution and attention configurations
-    (weak scaling: every rank runs the full configuration)."""
+    """TFLOP/s of each convolution / attention / GEMM / encoder workload at
+    its FIXED size, sharded across the ranks (strong scaling): images of C1,
+    C3 and C5 by batch, (batch, head) pairs of C4 and of the decode case, rows
+    of the GEMM.  Each rank builds and runs only its own shard; the time is
+    the max over ranks and the FLOPs are those of the whole problem."""
     import torch
 
     from forma_b200.api import AttentionOptions, ConvOptions
+    from forma_b200.shard import shard_range
 
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
@@ -294,91 +316,152 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     res = {}
     fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # FMA lanes x 2 FLOP x max clock
 
-    def record(name, fn, flops, peak, peak_name, note=None, nbytes=None):
-        """`nbytes`: algorithmic HBM bytes per call (inputs read once, outputs
-        written once); adds the fraction of measured HBM bandwidth and which
-        roof is the nearer one."""
+    def mine(total):
+        """This rank's [begin, end) of `total` units and the unit count."""
+        b, e = shard_range(total, dist.world, dist.rank)
+        return b, e, e - b
+
+    def record(name, fn, flops, peak, peak_name, note=None, nbytes=None, shard=None):
+        """`flops` / `nbytes`: the whole fixed problem's algorithmic FLOPs and
+        HBM bytes (inputs read once, outputs written once); the time is the
+        slowest rank's, so the rate is the job's."""
         for _ in range(2):
             fn()
         torch.cuda.synchronize(dev)
         dist.barrier()
         ms = dist.max(time_op(torch, fn, iters, flush, stream))
         tf = flops / (ms / 1e3) / 1e12
-        res[name] = {"tflops": round(dist.sum(tf), 2), "ms": round(ms, 4), "flop_per_call": flops,
-                     "roofline_frac": round(tf / peak, 4), "peak_tflops": round(peak, 1), "peak": peak_name}
+        res[name] = {"tflops": round(tf, 2), "ms": round(ms, 4), "flop_per_call": flops,
+                     "roofline_frac": round(tf / peak / dist.world, 4), "peak_tflops": round(peak, 1),
+                     "peak": peak_name + (f" per GPU, x{dist.world} GPUs" if dist.world > 1 else ""),
+                     "scaling": "strong", "shard": shard}
         if nbytes:
             gbs = nbytes / (ms / 1e3) / 1e9
-            res[name].update({"bytes_per_call": nbytes, "hbm_gbs": round(dist.sum(gbs), 1),
-                              "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+            res[name].update({"bytes_per_call": nbytes, "hbm_gbs": round(gbs, 1),
+                              "hbm_frac": round(gbs / pk["hbm_gbs"] / dist.world, 4),
                               "bound": "hbm" if gbs / pk["hbm_gbs"] > tf / peak else "tensor"})
         if note:
             res[name]["note"] = note
 
-    # C1: conv2d fp32 NCHW [8,64,56,56] x [64,64,3,3], stride 1, pad 1 (bit-faithful f32 path)
-    x = torch.rand(8, 64, 56, 56, device=dev, generator=g) * 2 - 1
+    def blank(*shape, dtype=torch.float32):
+        return torch.empty(*shape, dtype=dtype, device=dev)
+
+    # C1: conv2d fp32 NCHW [8,64,56,56] x [64,64,3,3], stride 1, pad 1 (bit-faithful f32 path), images sharded
+    b0, b1, n = mine(8)
+    x = torch.rand(max(n, 1), 64, 56, 56, device=dev, generator=g) * 2 - 1
     w = torch.randn(64, 64, 3, 3, device=dev, generator=g) * math.sqrt(2 / 576)
     o = ConvOptions([1, 1], [1, 1], [1, 1], [1, 1])
-    record("conv_f32_c1", lambda: api.conv(x, w, o), 2 * 8 * 64 * 56 * 56 * 64 * 9, fp32_peak,
-           "fp32 FMA peak (148 SMs x 128 lanes x 2 x max clock)",
-           "separate f32 multiply and add (reference order), so half the FMA peak is this kernel's ceiling")
+    record("conv_f32_c1", (lambda: api.conv(x[:n], w, o)) if n else (lambda: None), 2 * 8 * 64 * 56 * 56 * 64 * 9,
+           fp32_peak, "fp32 FMA peak (148 SMs x 128 lanes x 2 x max clock)",
+           "separate f32 multiply and add (reference order), so half the FMA peak is this kernel's ceiling",
+           shard=f"images {b0}:{b1} of 8 on this rank")
     del x, w
-    # C3a/C3b: ResNet-50 stage convs, bf16 NHWC, batch 256, f32 output
+    # C3a/C3b: ResNet-50 stage convs, bf16 NHWC, batch 256 sharded by image, f32 output
+    b0, b1, n = mine(256)
     for name, cin, k, pad in (("conv_bf16_3x3_c3a", 256, 3, 1), ("conv_bf16_1x1_c3b", 1024, 1, 0)):
-        xn = torch.randn(256, 14, 14, cin, device=dev, generator=g).bfloat16()
+        xn = torch.randn(n, 14, 14, cin, device=dev, generator=g).bfloat16()
         wn = (torch.randn(256, k, k, cin, device=dev, generator=g) * math.sqrt(2 / (cin * k * k))).bfloat16()
         xv, wv = xn.permute(0, 3, 1, 2), wn.permute(0, 3, 1, 2)  # NHWC / OHWI storage, logical NCHW / OIHW
-        out = torch.empty(256, 256, 14, 14, device=dev)  # contiguous f32 [N, O, P, Q], as the reference allocates
+        out = blank(n, 256, 14, 14)  # contiguous f32 [N, O, P, Q], as the reference allocates
         oc = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
         record(name, lambda: api.conv_low_f32_into(xv, wv, oc, out), 2 * 256 * 14 * 14 * 256 * cin * k * k,
                pk["bf16_tflops"], "measured bf16 dense (burst)",
-               nbytes=xn.numel() * 2 + wn.numel() * 2 + out.numel() * 4)
+               nbytes=256 * 14 * 14 * cin * 2 + wn.numel() * 2 * dist.world + 256 * 256 * 14 * 14 * 4,
+               shard=f"images {b0}:{b1} of 256 on this rank")
         del xn, wn, out
-    # C4: causal attention bf16 [8, 32, 4096, 128], scale 1/sqrt(128), f32 output
-    q = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
-    k = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
-    v = torch.randn(8, 32, 4096, 128, device=dev, generator=g).bfloat16()
+    # C4: causal attention bf16 [8, 32, 4096, 128], scale 1/sqrt(128), f32 output; the 256 (batch, head)
+    # pairs sharded as heads of a [pairs, L, D] view
     L = 4096
-    record("attention_bf16_causal_c4", lambda: api.attention_low_f32(q, k, v, None, AttentionOptions(causal=0)),
+    p0, p1, n = mine(8 * 32)
+    q, k, v = (torch.randn(n, L, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    o4 = blank(n, L, 128)
+    record("attention_bf16_causal_c4", lambda: api.attention_low_f32_into(q, k, v, None, AttentionOptions(causal=0), o4),
            4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
-           "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2", nbytes=3 * q.numel() * 2 + q.numel() * 4)
-    del q, k, v
+           "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2", nbytes=8 * 32 * L * 128 * (3 * 2 + 4),
+           shard=f"(batch, head) pairs {p0}:{p1} of 256 on this rank")
+    del q, k, v, o4
     # decode: one query per head, 32 query heads over 8 key/value heads, 8192 keys, bf16 (HBM-bound:
-    # reads K and V once)
-    q = torch.randn(8, 32, 1, 128, device=dev, generator=g).bfloat16()
-    k = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
-    v = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
-    record("attention_bf16_decode_gqa", lambda: api.attention_low_f32(q, k, v, None, AttentionOptions()),
+    # reads K and V once); batches sharded
+    b0, b1, n = mine(8)
+    q = torch.randn(max(n, 1), 32, 1, 128, device=dev, generator=g).bfloat16()
+    k = torch.randn(max(n, 1), 8, 8192, 128, device=dev, generator=g).bfloat16()
+    v = torch.randn(max(n, 1), 8, 8192, 128, device=dev, generator=g).bfloat16()
+    record("attention_bf16_decode_gqa",
+           (lambda: api.attention_low_f32(q[:n], k[:n], v[:n], None, AttentionOptions())) if n else (lambda: None),
            4 * 8 * 32 * 1 * 8192 * 128, pk["bf16_tflops"], "measured bf16 dense (burst)",
            "GQA heads packed into one tile per key/value head, key range split across CTAs",
-           nbytes=2 * k.numel() * 2 + q.numel() * 2 + 8 * 32 * 128 * 4)
+           nbytes=2 * 8 * 8 * 8192 * 128 * 2 + 8 * 32 * 128 * 2 + 8 * 32 * 128 * 4, shard=f"batches {b0}:{b1} of 8")
     del q, k, v
-    # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32 output
-    a = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
+    # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32
+    # output, rows of the left operand sharded
+    r0, r1, n = mine(8192)
+    a = torch.randn(n, 8192, device=dev, generator=g).bfloat16()
     b = torch.randn(8192, 8192, device=dev, generator=g).bfloat16()
-    c = torch.empty(8192, 8192, device=dev)
+    c = blank(n, 8192)
     record("matmul_bf16_8192", lambda: api.matmul_low_f32(a, b, out=c), 2 * 8192 ** 3, pk["bf16_tflops"],
            "measured bf16 dense (burst)", "row-major right operand (MN-major B); f32 output",
-           nbytes=a.numel() * 2 + b.numel() * 2 + c.numel() * 4)
+           nbytes=8192 * 8192 * (2 + 4) + b.numel() * 2 * dist.world, shard=f"rows {r0}:{r1} of 8192")
     del a, b, c
-    # C5: ViT-style encoder forward, [64,3,224,224] bf16, patch 16, 12 layers (E 768, H 12, D 64, L 197, MLP 3072)
+    # C5: ViT-style encoder forward, [64,3,224,224] bf16, patch 16, 12 layers (E 768, H 12, D 64, L 197,
+    # MLP 3072); the 64 images sharded, the same weights on every rank
     from forma_b200.vit import ViTConfig, ViTEncoder
 
     cfg = ViTConfig()
-    enc = ViTEncoder(cfg, dev, seed=dist.rank)
-    img = torch.randn(cfg.batch, cfg.channels, cfg.image, cfg.image, device=dev, generator=g).bfloat16()
+    b0, b1, n = mine(cfg.batch)
+    enc = ViTEncoder(cfg, dev, seed=0)
+    img = torch.randn(n, cfg.channels, cfg.image, cfg.image, device=dev, generator=g).bfloat16()
     fl = cfg.flops()
     record("vit_encoder_c5", lambda: enc.forward(img), fl["total"], pk["bf16_tflops"], "measured bf16 dense (burst)",
            "random-init pre-norm encoder, LN eps 1e-5, tanh GELU; FLOPs = patch conv + per layer QKV/out/MLP "
-           "projections (1x1 convs) + attention 4*B*H*L^2*D; glue (casts, adds, LN) counted as time only")
+           "projections (1x1 convs) + attention 4*B*H*L^2*D; glue (casts, adds, LN) counted as time only",
+           shard=f"images {b0}:{b1} of {cfg.batch}")
     res["vit_encoder_c5"]["flops_by_stage"] = fl
-    # the same forward as a prepared program (one CUDA graph launch per forward)
+    # the same forward as a prepared program (one CUDA graph launch per forward, fb_program_*)
     from forma_b200.program import Program
 
     prog = Program(enc.forward, img, device=dev)
     record("vit_encoder_c5_graph", prog.run, fl["total"], pk["bf16_tflops"], "measured bf16 dense (burst)",
-           "the C5 forward captured once and replayed as one CUDA graph (forma_b200.program.Program)")
+           "the C5 forward recorded once and replayed as one CUDA graph (fb_program_*, forma_b200.program.Program)",
+           shard=f"images {b0}:{b1} of {cfg.batch}")
+    prog.close()
     del prog, enc, img
     return res
+
+
+def cpu_baseline_ops() -> dict:
+    """The oracle (the reference's f64 algorithms) on the host's cores on one
+    unit of each fixed problem, extrapolated per unit to the whole problem:
+    one image of C1 / C3a / C3b, one (batch, head) pair of C4."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    threads = orc.threads()
+    rng = np.random.default_rng(0)
+    out = {}
+
+    def timed(fn):
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    x = rng.uniform(-1, 1, (1, 64, 56, 56)).astype(np.float32)
+    w = (rng.standard_normal((64, 64, 3, 3)) * math.sqrt(2 / 576)).astype(np.float32)
+    dt = timed(lambda: orc.conv_f32_seq(x, w, [1, 1], [1, 1], [1, 1], [1, 1], 1, threads))
+    out["conv_f32_c1"] = {"tflops": 2 * 64 * 56 * 56 * 64 * 9 / dt / 1e12, "sample": "1 of 8 images, f32 reference order"}
+    for name, cin, k, pad in (("conv_bf16_3x3_c3a", 256, 3, 1), ("conv_bf16_1x1_c3b", 1024, 1, 0)):
+        x = rng.standard_normal((1, cin, 14, 14)).astype(np.float32)
+        w = rng.standard_normal((256, cin, k, k)).astype(np.float32)
+        dt = timed(lambda: orc.conv(x, w, [1, 1], [1, 1], [pad, pad], [pad, pad], 1, threads))
+        out[name] = {"tflops": 2 * 14 * 14 * 256 * cin * k * k / dt / 1e12, "sample": "1 of 256 images, f64"}
+    q, kk, v = (rng.standard_normal((1, 1, 4096, 128)).astype(np.float32) for _ in range(3))
+    dt = timed(lambda: orc.attention(q, kk, v, None, None, 0, threads))
+    out["attention_bf16_causal_c4"] = {"tflops": 4 * 128 * 4096 * 4097 // 2 / dt / 1e12,
+                                       "sample": "1 of 256 (batch, head) pairs, f64 dense attention"}
+    for v_ in out.values():
+        v_["tflops"] = round(v_["tflops"], 5)
+        v_.update({"cores": threads, "kind": "port", "extrapolated": True})
+    return out
 
 
 # ------------------------------------------------------------------ main
@@ -409,7 +492,7 @@ def run_forma(args) -> int:
     per_kernel_ms = {k: 0.0 for k in bytes_per}
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     class _Local:
-        pg = None  # no collective: ranks may run different numbers of busy steps
+        comm = None  # no collective: ranks may run different numbers of busy steps
 
     def busy():
         row_ops(api, x, _Local)
@@ -455,6 +538,8 @@ def run_forma(args) -> int:
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
         cpu = cpu_baseline_rows(args.cpu_rows)
+        if not args.no_ops:
+            cpu["ops"] = cpu_baseline_ops()
     return emit(args, dist, pk, value, total_ms, step_bytes, dom, achieved, traffic, per_kernel_ms, bytes_per, e2e,
                 launches, clocks, cpu, ops, rows)
 
@@ -565,7 +650,8 @@ def run_reference(args) -> int:
     dt = (time.perf_counter() - t0) / args.steps
     value = b / dt / 1e9
     sample = (f"{rows} of {ROWS} rows x {COLS} f32 per step through sum, max, argmax, softmax, moments, global sum "
-              f"(oracle port of the reference's f64 algorithms, {threads} threads)")
+              f"(oracle port of the reference's f64 algorithms, {threads} threads); GB/s extrapolated per byte "
+              f"from the {rows}-row sample to the {ROWS}-row workload")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -581,7 +667,8 @@ def run_reference(args) -> int:
         "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": "row reductions: X [65536, 4096] f32 ~N(0,1); per-row sum, max, argmax, softmax, "
-                               "layer-norm moments; global sum", "rows_per_gpu": ROWS, "cols": COLS},
+                               "layer-norm moments; global sum", "rows_per_gpu": ROWS, "cols": COLS,
+                   "sample_rows": rows, "extrapolated": True},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

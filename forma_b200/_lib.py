@@ -37,6 +37,10 @@ STATUS_NAMES = {
     33: "Dtype",
     34: "Driver",
     35: "Unsupported",
+    36: "ForeignRuntime",
+    37: "MissingSymbol",
+    38: "Graph",
+    39: "ProgramPoisoned",
 }
 
 
@@ -86,6 +90,7 @@ SIGNATURES = {
     "fb_status_string": (C.c_char_p, [C.c_int]),
     "fb_last_error": (C.c_char_p, []),
     "fb_launch_count": (C.c_uint64, []),
+    "fb_last_route": (C.c_char_p, []),
     "fb_device_status": (C.c_uint32, []),
     "fb_conv_plan": (C.c_int, [U64P, C.c_uint32, U64P, C.c_uint32, C.POINTER(FbConvOptions), U64P, U32P]),
     "fb_conv": (C.c_int, [T, T, C.POINTER(FbConvOptions), T, VP]),
@@ -120,7 +125,20 @@ SIGNATURES = {
     "fb_matmul_low": (C.c_int, [T, T, T, VP]),
     "fb_add": (C.c_int, [T, T, T, VP]),
     "fb_gelu_to_low": (C.c_int, [T, T, VP]),
+    "fb_global_sum_nccl": (C.c_int, [T, VP, T, VP]),
+    "fb_nccl_unique_id": (C.c_int, [VP]),
+    "fb_nccl_comm_init_rank": (C.c_int, [C.POINTER(VP), C.c_int, VP, C.c_int]),
+    "fb_nccl_comm_init_all": (C.c_int, [C.POINTER(VP), C.c_int, C.POINTER(C.c_int)]),
+    "fb_nccl_comm_destroy": (C.c_int, [VP]),
+    "fb_program_begin": (C.c_int, [VP]),
+    "fb_program_end": (C.c_int, [VP, C.POINTER(VP)]),
+    "fb_program_launch": (C.c_int, [VP, VP]),
+    "fb_program_stats": (C.c_int, [VP, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_int32)]),
+    "fb_program_destroy": (C.c_int, [VP]),
+    "fb_selftest_bounded_wait": (C.c_int, [C.c_uint64, VP]),
 }
+
+NCCL_UNIQUE_ID_BYTES = 128
 
 _lib = None
 

@@ -133,13 +133,44 @@ def _stream(device: torch.device):
     return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+class _on:
+    """Makes `device` current around one C call (every entry point runs on the
+    current device, which must own its operands and stream) and restores the
+    previous device afterwards; a no-op when it is current already."""
+
+    __slots__ = ("device", "prev")
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.prev = None
+
+    def __enter__(self) -> torch.device:
+        cur = torch.cuda.current_device()
+        if cur != self.device.index:
+            self.prev = cur
+            torch.cuda.set_device(self.device)
+        return self.device
+
+    def __exit__(self, *exc) -> None:
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
 def _device(*ts: torch.Tensor) -> torch.device:
+    """The one CUDA device that holds every given tensor."""
+    dev = None
     for t in ts:
-        if t is not None:
-            if t.device.type != "cuda":
-                raise TensorError(32, "tensors must be CUDA device memory (no CPU fallback)")
-            return t.device
-    raise TensorError(32, "no tensor")
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise TensorError(32, "tensors must be CUDA device memory (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise TensorError(36, f"operands on {dev} and {t.device}: one call runs on one device")
+    if dev is None:
+        raise TensorError(32, "no tensor")
+    return dev
 
 
 def _conv_options(o: ConvOptions):
@@ -205,7 +236,8 @@ def _conv(fn, input, weight, options, out_dtype):
     dims = conv_plan(list(input.shape), list(weight.shape), options)
     out = torch.empty(dims, dtype=out_dtype, device=dev)
     di, dw, do = describe(input), describe(weight), describe(out)
-    _check(fn(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(fn(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -226,39 +258,43 @@ def conv_low(input: torch.Tensor, weight: torch.Tensor, options: ConvOptions) ->
 
 def conv_low_f32_into(input, weight, options, out):
     """conv_low_f32 into a caller-provided output view (e.g. a channels-last permuted view)."""
-    dev = _device(input, weight)
+    dev = _device(input, weight, out)
     opts, _keep = _conv_options(options)
     di, dw, do = describe(input), describe(weight), describe(out)
-    _check(lib().fb_conv_low_f32(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_conv_low_f32(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev_)))
     return out
 
 
 def conv_low_into(input, weight, options, out):
     """conv_low into a caller-provided 16-bit output view (e.g. channels-last)."""
-    dev = _device(input, weight)
+    dev = _device(input, weight, out)
     opts, _keep = _conv_options(options)
     di, dw, do = describe(input), describe(weight), describe(out)
-    _check(lib().fb_conv_low(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_conv_low(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev_)))
     return out
 
 
 def conv_low_gelu_into(input, weight, options, out):
     """gelu_to_low(conv_low_f32(input, weight)) into a 16-bit output view, the
     GELU applied in the tensor-core GEMM's epilogue (bit-identical)."""
-    dev = _device(input, weight)
+    dev = _device(input, weight, out)
     opts, _keep = _conv_options(options)
     di, dw, do = describe(input), describe(weight), describe(out)
-    _check(lib().fb_conv_low_gelu(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_conv_low_gelu(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev_)))
     return out
 
 
 def conv_low_f32_accumulate(input, weight, options, out):
     """out += conv_low_f32(input, weight) in place (f32 output view): a
     residual connection folded into the GEMM epilogue (bit-identical to add)."""
-    dev = _device(input, weight)
+    dev = _device(input, weight, out)
     opts, _keep = _conv_options(options)
     di, dw, do = describe(input), describe(weight), describe(out)
-    _check(lib().fb_conv_low_f32_accumulate(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_conv_low_f32_accumulate(C.byref(di), C.byref(dw), C.byref(opts), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -274,11 +310,12 @@ def matmul_plan(left_shape: Sequence[int], right_shape: Sequence[int]) -> list:
 
 
 def _matmul(fn, left, right, out_dtype, out=None):
-    dev = _device(left, right)
+    dev = _device(left, right, out)
     if out is None:
         out = torch.empty(matmul_plan(list(left.shape), list(right.shape)), dtype=out_dtype, device=dev)
     dl, dr, do = describe(left), describe(right), describe(out)
-    _check(fn(C.byref(dl), C.byref(dr), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(fn(C.byref(dl), C.byref(dr), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -296,7 +333,7 @@ def matmul_low(left: torch.Tensor, right: torch.Tensor, out: Optional[torch.Tens
 
 def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOptions, out=None,
                out_dtype=torch.float32):
-    dev = _device(query, key, value)
+    dev = _device(query, key, value, out, mask.tensor if mask is not None else None)
     kind = 0
     dm = None
     if mask is not None:
@@ -310,8 +347,9 @@ def _attention(fn, query, key, value, mask: Optional[Mask], options: AttentionOp
         dm = describe(mask.tensor)
         if mask.kind == "keep":
             dm.dtype = _lib.U32
-    _check(fn(C.byref(dq), C.byref(dk), C.byref(dv), kind, C.byref(dm) if dm is not None else None,
-              _attn_options(options), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(fn(C.byref(dq), C.byref(dk), C.byref(dv), kind, C.byref(dm) if dm is not None else None,
+                  _attn_options(options), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -354,9 +392,11 @@ def _reduce(fn, op, input, axes, keep_dims, mean, out_dtype):
             di.dtype = _lib.U32
     ax = _lib.u32_array(axes)
     if mean:
-        _check(fn(C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev_)))
     else:
-        _check(fn(int(op), C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(int(op), C.byref(di), ax, len(axes), int(keep_dims), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -380,7 +420,8 @@ def argmax(input: torch.Tensor, axis: int, keep_dims: bool = False) -> torch.Ten
     out = torch.empty(dims, dtype=torch.int32, device=dev)
     di, do = describe(input), describe(out)
     do.dtype = _lib.U32
-    _check(lib().fb_argmax(C.byref(di), axis, int(keep_dims), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_argmax(C.byref(di), axis, int(keep_dims), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -390,27 +431,72 @@ def sum_partial_f64(input: torch.Tensor, partial: Optional[torch.Tensor] = None)
     if partial is None:
         partial = torch.empty((), dtype=torch.float64, device=dev)
     di = describe(input)
-    _check(lib().fb_sum_partial_f64(C.byref(di), C.c_void_p(partial.data_ptr()), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_sum_partial_f64(C.byref(di), C.c_void_p(partial.data_ptr()), _stream(dev_)))
     return partial
 
 
 def finish_sum(partial: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    dev = _device(partial)
+    dev = _device(partial, out)
     if out is None:
         out = torch.empty((), dtype=torch.float32, device=dev)
     do = describe(out)
-    _check(lib().fb_finish_sum_f64(C.c_void_p(partial.data_ptr()), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_finish_sum_f64(C.c_void_p(partial.data_ptr()), C.byref(do), _stream(dev_)))
     return out
 
 
-def global_sum(shard: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum over all elements of all ranks' shards: local f64 partial, one
-    8-byte all-reduce over `group` (only when a group is given: every rank of
-    the group must make the same call), then f32 rounding."""
-    partial = sum_partial_f64(shard)
-    if group is not None:
-        torch.distributed.all_reduce(partial, group=group)
-    return finish_sum(partial)
+class NcclCommunicator:
+    """An NCCL communicator of one device, created and used through the C ABI
+    (``fb_nccl_*``), for :func:`global_sum` across GPUs."""
+
+    def __init__(self, handle: C.c_void_p, device: torch.device):
+        self.handle, self.device = handle, device
+
+    @staticmethod
+    def unique_id() -> bytes:
+        """A fresh NCCL unique id (rank 0 makes it and hands it to the others)."""
+        buf = (C.c_char * _lib.NCCL_UNIQUE_ID_BYTES)()
+        _check(lib().fb_nccl_unique_id(buf))
+        return bytes(buf)
+
+    @classmethod
+    def init_rank(cls, nranks: int, unique_id: bytes, rank: int, device) -> "NcclCommunicator":
+        """Joins rank `rank` of `nranks` on `device` (every rank calls this)."""
+        device = torch.device(device)
+        if len(unique_id) != _lib.NCCL_UNIQUE_ID_BYTES:
+            raise TensorError(32, "an NCCL unique id has 128 bytes")
+        uid = (C.c_char * _lib.NCCL_UNIQUE_ID_BYTES).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        with _on(device):
+            _check(lib().fb_nccl_comm_init_rank(C.byref(h), nranks, uid, rank))
+        return cls(h, device)
+
+    def destroy(self) -> None:
+        if self.handle is not None and self.handle.value:
+            with _on(self.device):
+                _check(lib().fb_nccl_comm_destroy(self.handle))
+        self.handle = None
+
+
+def global_sum(shard: torch.Tensor, comm: Optional[NcclCommunicator] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Sum over all elements of every rank's shard, rounded to f32 (a 0-d
+    tensor).  With a communicator: ``fb_global_sum_nccl`` - this shard's f64
+    partial, one 8-byte NCCL all-reduce and the rounding, all on the C side
+    and the current stream (every rank of the communicator makes the call).
+    Without one: this shard alone."""
+    dev = _device(shard, out)
+    if out is None:
+        out = torch.empty((), dtype=torch.float32, device=dev)
+    if comm is None:
+        return finish_sum(sum_partial_f64(shard), out)
+    if comm.device != dev:
+        raise TensorError(36, f"communicator of {comm.device}, shard on {dev}")
+    di, do = describe(shard), describe(out)
+    with _on(dev) as dev_:
+        _check(lib().fb_global_sum_nccl(C.byref(di), comm.handle, C.byref(do), _stream(dev_)))
+    return out
 
 
 # ------------------------------------------------------------- statistics
@@ -421,9 +507,11 @@ def _normalize(fn, input, axes, eps=None):
     di, do = describe(input), describe(out)
     ax = _lib.u32_array(axes)
     if eps is None:
-        _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev_)))
     else:
-        _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -440,15 +528,17 @@ def layer_norm(input: torch.Tensor, axes: Sequence[int], epsilon: float) -> torc
 
 
 def _normalize_low(fn, input, axes, dtype, eps=None, out=None):
-    dev = _device(input)
+    dev = _device(input, out)
     if out is None:
         out = torch.empty(list(input.shape), dtype=dtype, device=dev)
     ax = _lib.u32_array(axes)
     di, do = describe(input), describe(out)
     if eps is None:
-        _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(C.byref(di), ax, len(axes), C.byref(do), _stream(dev_)))
     else:
-        _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev)))
+        with _on(dev) as dev_:
+            _check(fn(C.byref(di), ax, len(axes), C.c_float(eps), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -474,7 +564,8 @@ def logsumexp(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False)
     dims = reduce_shape(ReduceOp.Sum, list(input.shape), list(axes), keep_dims, True)
     out = torch.empty(dims, dtype=torch.float32, device=dev)
     di, do = describe(input), describe(out)
-    _check(lib().fb_logsumexp(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_logsumexp(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -484,8 +575,9 @@ def moments(input: torch.Tensor, axes: Sequence[int], keep_dims: bool = False) -
     mean = torch.empty(dims, dtype=torch.float32, device=dev)
     var = torch.empty(dims, dtype=torch.float32, device=dev)
     di, dm, dv = describe(input), describe(mean), describe(var)
-    _check(lib().fb_moments(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(dm), C.byref(dv),
-                            _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_moments(C.byref(di), _lib.u32_array(axes), len(axes), int(keep_dims), C.byref(dm), C.byref(dv),
+                                _stream(dev_)))
     return Moments(mean, var)
 
 
@@ -501,14 +593,16 @@ def cast_to_low(input: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     dev = _device(input)
     out = torch.empty(list(input.shape), dtype=dtype, device=dev)
     di, do = describe(input), describe(out)
-    _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(dev)))
+    with _on(dev) as dev_:
+        _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(dev_)))
     return out
 
 
 def cast_to_low_into(input: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """cast_to_low into a caller-owned contiguous tensor (chains reuse buffers)."""
     di, do = describe(input), describe(out)
-    _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(_device(input, out))))
+    with _on(_device(input, out)) as dev_:
+        _check(lib().fb_cast_to_low(C.byref(di), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -520,7 +614,8 @@ def add(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None) ->
     if out is None:
         out = torch.empty(list(a.shape), dtype=torch.float32, device=_device(a, b))
     da, db, do = describe(a), describe(b), describe(out)
-    _check(lib().fb_add(C.byref(da), C.byref(db), C.byref(do), _stream(_device(a, b, out))))
+    with _on(_device(a, b, out)) as dev_:
+        _check(lib().fb_add(C.byref(da), C.byref(db), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -529,7 +624,8 @@ def gelu_to_low(input: torch.Tensor, dtype: torch.dtype, out: Optional[torch.Ten
     if out is None:
         out = torch.empty(list(input.shape), dtype=dtype, device=_device(input))
     di, do = describe(input), describe(out)
-    _check(lib().fb_gelu_to_low(C.byref(di), C.byref(do), _stream(_device(input, out))))
+    with _on(_device(input, out)) as dev_:
+        _check(lib().fb_gelu_to_low(C.byref(di), C.byref(do), _stream(dev_)))
     return out
 
 
@@ -538,6 +634,21 @@ def device_status() -> int:
     return int(lib().fb_device_status())
 
 
+def selftest_bounded_wait(limit_ns: int, device=None) -> None:
+    """Enqueues a kernel whose bounded wait on an mbarrier nothing arrives at
+    gives up after `limit_ns`; the timeout then shows in device_status()."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with _on(dev) as dev_:
+        _check(lib().fb_selftest_bounded_wait(int(limit_ns), _stream(dev_)))
+
+
 def launch_count() -> int:
     """Kernel launches this library has enqueued."""
     return int(lib().fb_launch_count())
+
+
+def last_route() -> list:
+    """Kernels the most recent call on this thread enqueued, in launch order
+    (e.g. ``["conv_gemm_pair_kernel<192,8>"]``)."""
+    r = lib().fb_last_route().decode()
+    return r.split(",") if r else []

@@ -59,7 +59,7 @@ def _compile(src: Path, obj: Path) -> None:
     if src.suffix == ".cu":
         cmd += CUDA_FLAGS
     else:
-        cmd += ["-x", "c++"]
+        cmd += ["-x", "c++", "-Wno-deprecated-gpu-targets"]
     subprocess.run(cmd, check=True)
 
 
@@ -79,7 +79,7 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
     if force or todo or _stale(LIB, objs):
         tmp = LIB.with_suffix(".so.tmp")
         subprocess.run(
-            [NVCC, "-shared", "-o", str(tmp)] + ARCH + [str(o) for o in objs] + ["-cudart", "static", "-lpthread"],
+            [NVCC, "-shared", "-o", str(tmp)] + ARCH + [str(o) for o in objs] + ["-cudart", "static", "-lpthread", "-ldl"],
             check=True,
         )
         os.replace(tmp, LIB)

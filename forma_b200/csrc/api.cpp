@@ -26,6 +26,10 @@ namespace {
 
 std::atomic<uint64_t> g_launches{0};
 thread_local std::string g_driver_error;
+// Kernels enqueued by the current (or most recent) entry-point call of this
+// host thread, comma-separated in launch order.
+thread_local std::string g_route;
+thread_local uint64_t g_thread_launches = 0;
 
 struct ScratchBlock {
     void* ptr = nullptr;
@@ -573,6 +577,18 @@ int attention_impl(const fb_tensor* q, const fb_tensor* k, const fb_tensor* v, u
     return finish(launched(s, "attention"));
 }
 
+// f64 sum of every element of an f32 view into the device double `partial`
+// (zero for an empty view).
+int sum_partial_of(const View& in, double* partial, void* stream) {
+    if (in.count == 0) {
+        if (cudaMemsetAsync(partial, 0, sizeof(double), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+            return fail(FB_ERR_DRIVER, "memset failed");
+        return FB_OK;
+    }
+    Rows rows = make_rows(in, all_axes(in.dims.size()));
+    return launched(launch_sum_partial(rows, partial, stream), "sum partial");
+}
+
 // MatmulPlan::new (tensor-core/src/shape.rs:148-192).
 struct MatmulPlanH {
     Dims left, right;      // vector operands promoted to matrices
@@ -689,7 +705,29 @@ int sm_count() {
     return cached[dev];
 }
 
-void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_launch(const char* kernel) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    ++g_thread_launches;
+    if (!g_route.empty()) g_route += ',';
+    g_route += kernel;
+}
+
+std::string kernel_name(const char* base, std::initializer_list<int> params) {
+    std::string s(base);
+    s += '<';
+    bool first = true;
+    for (int v : params) {
+        if (!first) s += ',';
+        s += std::to_string(v);
+        first = false;
+    }
+    s += '>';
+    return s;
+}
+
+void begin_route() { g_route.clear(); }
+
+uint64_t thread_launch_count() { return g_thread_launches; }
 
 int launch_status(const char* what) {
     const cudaError_t e = cudaGetLastError();
@@ -701,8 +739,14 @@ int launch_status(const char* what) {
 void* scratch(void* stream, uint64_t bytes, int slot) {
     int dev = 0;
     cudaGetDevice(&dev);
+    // cudaStreamPerThread is one handle value naming a different stream in
+    // every host thread: key its scratch by thread so that concurrent threads
+    // never share a block.  (The legacy default stream is one stream for all
+    // threads; its work is ordered, so sharing its block is safe.)
+    static thread_local char per_thread_key;
+    void* key = stream == static_cast<void*>(cudaStreamPerThread) ? static_cast<void*>(&per_thread_key) : stream;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    ScratchBlock& b = g_scratch[std::make_tuple(dev, stream, slot)];
+    ScratchBlock& b = g_scratch[std::make_tuple(dev, key, slot)];
     if (b.bytes >= bytes) return b.ptr;
     // No allocation while the stream is being captured into a graph (it would
     // invalidate the capture): an eager call on the stream must come first.
@@ -753,6 +797,10 @@ const char* fb_status_string(int status) {
         case FB_ERR_DTYPE: return "tensor dtype mismatch";
         case FB_ERR_DRIVER: return "CUDA driver error";
         case FB_ERR_UNSUPPORTED: return "unsupported";
+        case FB_ERR_FOREIGN_RUNTIME: return "tensor belongs to a different device";
+        case FB_ERR_MISSING_SYMBOL: return "incompatible library: missing symbol";
+        case FB_ERR_GRAPH: return "CUDA graph error";
+        case FB_ERR_PROGRAM_POISONED: return "prepared program is poisoned after an execution error";
         default: return "unknown status";
     }
 }
@@ -760,6 +808,8 @@ const char* fb_status_string(int status) {
 const char* fb_last_error(void) { return last_error_cstr(); }
 
 uint64_t fb_launch_count(void) { return g_launches.load(); }
+
+const char* fb_last_route(void) { return g_route.c_str(); }
 
 uint32_t fb_device_status(void) {
     cudaDeviceSynchronize();
@@ -791,35 +841,42 @@ int fb_matmul_plan(const uint64_t* left_dims, uint32_t left_rank, const uint64_t
 }
 
 int fb_matmul_low_f32(const fb_tensor* left, const fb_tensor* right, fb_tensor* output, void* stream) {
+    begin_route();
     return matmul_impl(left, right, output, stream, false);
 }
 
 int fb_matmul_low(const fb_tensor* left, const fb_tensor* right, fb_tensor* output, void* stream) {
+    begin_route();
     return matmul_impl(left, right, output, stream, true);
 }
 
 int fb_conv(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
             void* stream) {
+    begin_route();
     return conv_impl(input, weight, options, output, stream, false, false);
 }
 
 int fb_conv_low_f32(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
                     void* stream) {
+    begin_route();
     return conv_impl(input, weight, options, output, stream, true, false);
 }
 
 int fb_conv_low(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
                 void* stream) {
+    begin_route();
     return conv_impl(input, weight, options, output, stream, true, true);
 }
 
 int fb_conv_low_gelu(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options, fb_tensor* output,
                      void* stream) {
+    begin_route();
     return conv_impl(input, weight, options, output, stream, true, true, CONV_EPI_GELU);
 }
 
 int fb_conv_low_f32_accumulate(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options,
                                fb_tensor* output, void* stream) {
+    begin_route();
     return conv_impl(input, weight, options, output, stream, true, false, CONV_EPI_ACCUMULATE);
 }
 
@@ -842,16 +899,19 @@ int fb_attention_plan(const uint64_t* q_dims, uint32_t q_rank, const uint64_t* k
 
 int fb_attention(const fb_tensor* query, const fb_tensor* key, const fb_tensor* value, uint32_t mask_kind,
                  const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream) {
+    begin_route();
     return attention_impl(query, key, value, mask_kind, mask, options, output, stream, false);
 }
 
 int fb_attention_low_f32(const fb_tensor* query, const fb_tensor* key, const fb_tensor* value, uint32_t mask_kind,
                          const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream) {
+    begin_route();
     return attention_impl(query, key, value, mask_kind, mask, options, output, stream, true);
 }
 
 int fb_attention_low(const fb_tensor* query, const fb_tensor* key, const fb_tensor* value, uint32_t mask_kind,
                      const fb_tensor* mask, fb_attention_options options, fb_tensor* output, void* stream) {
+    begin_route();
     return attention_impl(query, key, value, mask_kind, mask, options, output, stream, true, true);
 }
 
@@ -867,20 +927,24 @@ int fb_reduce_shape(uint32_t op, const uint64_t* dims, uint32_t rank, const uint
 
 int fb_reduce_f32(uint32_t op, const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, int32_t keep_dims,
                   fb_tensor* output, void* stream) {
+    begin_route();
     return reduce_impl(op, input, axes, n_axes, keep_dims, output, stream, FB_F32, false);
 }
 
 int fb_reduce_u32(uint32_t op, const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, int32_t keep_dims,
                   fb_tensor* output, void* stream) {
+    begin_route();
     return reduce_impl(op, input, axes, n_axes, keep_dims, output, stream, FB_U32, false);
 }
 
 int fb_mean_axes(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, int32_t keep_dims, fb_tensor* output,
                  void* stream) {
+    begin_route();
     return reduce_impl(FB_REDUCE_SUM, input, axes, n_axes, keep_dims, output, stream, FB_F32, true);
 }
 
 int fb_argmax(const fb_tensor* input, uint32_t axis, int32_t keep_dims, fb_tensor* output, void* stream) {
+    begin_route();
     View in, out;
     FB_TRY(view_of(input, "input", &in));
     if (in.dtype != FB_F32) return fail(FB_ERR_DTYPE, "argmax input must be f32");
@@ -896,20 +960,31 @@ int fb_argmax(const fb_tensor* input, uint32_t axis, int32_t keep_dims, fb_tenso
 }
 
 int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream) {
+    begin_route();
     View in;
     FB_TRY(view_of(input, "input", &in));
     if (in.dtype != FB_F32) return fail(FB_ERR_DTYPE, "global sum input must be f32");
     if (!partial) return fail(FB_ERR_INVALID_INPUT, "null partial pointer");
-    Rows rows = make_rows(in, all_axes(in.dims.size()));
-    if (in.count == 0) {
-        if (cudaMemsetAsync(partial, 0, sizeof(double), static_cast<cudaStream_t>(stream)) != cudaSuccess)
-            return fail(FB_ERR_DRIVER, "memset failed");
-        return FB_OK;
-    }
-    return launched(launch_sum_partial(rows, partial, stream), "sum partial");
+    return sum_partial_of(in, partial, stream);
+}
+
+int fb_global_sum_nccl(const fb_tensor* shard, void* comm, fb_tensor* output, void* stream) {
+    begin_route();
+    View in, out;
+    FB_TRY(view_of(shard, "shard", &in));
+    if (in.dtype != FB_F32) return fail(FB_ERR_DTYPE, "global sum input must be f32");
+    FB_TRY(view_of(output, "output", &out));
+    if (out.dtype != FB_F32 || out.count != 1) return fail(FB_ERR_INVALID_INPUT, "global sum output must be one f32");
+    if (!comm) return fail(FB_ERR_INVALID_INPUT, "null communicator");
+    double* partial = static_cast<double*>(scratch(stream, 256, SCRATCH_COLLECTIVE));
+    if (!partial) return fail(FB_ERR_DRIVER, "scratch allocation failed");
+    if (int rc = sum_partial_of(in, partial, stream); rc != FB_OK) return rc;
+    if (int rc = nccl_all_reduce_sum_f64(partial, 1, comm, stream); rc != FB_OK) return rc;
+    return launched(launch_finish_sum(partial, static_cast<float*>(out.data) + out.offset, stream), "finish sum");
 }
 
 int fb_sum_partial_f64_static(const fb_tensor* input, double* partial, void* stream) {
+    begin_route();
     View in;
     FB_TRY(view_of(input, "input", &in));
     if (in.dtype != FB_F32) return fail(FB_ERR_DTYPE, "global sum input must be f32");
@@ -929,7 +1004,15 @@ int fb_sum_partial_f64_static(const fb_tensor* input, double* partial, void* str
 
 uint64_t fb_sum_static_max_elements(void) { return static_sum_max_elements(); }
 
+int fb_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+    begin_route();
+    if (limit_ns == 0 || limit_ns > 1000000000ull)
+        return fail(FB_ERR_INVALID_INPUT, "self-test wait limit must be in (0, 1e9] nanoseconds");
+    return launched(launch_selftest_wait(limit_ns, stream), "self-test wait");
+}
+
 int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream) {
+    begin_route();
     View out;
     FB_TRY(view_of(output, "output", &out));
     if (out.dtype != FB_F32 || out.count != 1) return fail(FB_ERR_INVALID_INPUT, "global sum output must be one f32");
@@ -938,29 +1021,35 @@ int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream) {
 }
 
 int fb_softmax(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, fb_tensor* output, void* stream) {
+    begin_route();
     return normalize_impl(STATS_SOFTMAX, input, axes, n_axes, 0.0f, output, stream);
 }
 
 int fb_log_softmax(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, fb_tensor* output, void* stream) {
+    begin_route();
     return normalize_impl(STATS_LOG_SOFTMAX, input, axes, n_axes, 0.0f, output, stream);
 }
 
 int fb_layer_norm(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, float epsilon, fb_tensor* output,
                   void* stream) {
+    begin_route();
     return normalize_impl(STATS_LAYER_NORM, input, axes, n_axes, epsilon, output, stream);
 }
 
 int fb_logsumexp(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, int32_t keep_dims, fb_tensor* output,
                  void* stream) {
+    begin_route();
     return row_stats_impl(STATS_LOGSUMEXP, input, axes, n_axes, keep_dims, output, nullptr, stream);
 }
 
 int fb_moments(const fb_tensor* input, const uint32_t* axes, uint32_t n_axes, int32_t keep_dims, fb_tensor* mean,
                fb_tensor* variance, void* stream) {
+    begin_route();
     return row_stats_impl(STATS_MOMENTS, input, axes, n_axes, keep_dims, mean, variance, stream);
 }
 
 int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream) {
+    begin_route();
     View in, out;
     FB_TRY(view_of(input, "input", &in));
     FB_TRY(view_of(output, "output", &out));
@@ -974,6 +1063,7 @@ int fb_cast_to_low(const fb_tensor* input, fb_tensor* output, void* stream) {
 }
 
 int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stream) {
+    begin_route();
     View x, y, out;
     FB_TRY(view_of(a, "a", &x));
     FB_TRY(view_of(b, "b", &y));
@@ -1045,6 +1135,7 @@ int fb_add(const fb_tensor* a, const fb_tensor* b, fb_tensor* output, void* stre
 }
 
 int fb_gelu_to_low(const fb_tensor* input, fb_tensor* output, void* stream) {
+    begin_route();
     View in, out;
     FB_TRY(view_of(input, "input", &in));
     FB_TRY(view_of(output, "output", &out));

@@ -22,6 +22,7 @@ enum DeviceStatus : uint32_t {
     DEV_GEMM_MMA_TIMEOUT = 3,
     DEV_GEMM_EPILOGUE_TIMEOUT = 4,
     DEV_ATTN_TIMEOUT = 5,
+    DEV_SELFTEST_TIMEOUT = 6,  // fb_selftest_bounded_wait: the wait gave up as intended
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -66,13 +67,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the barrier phase with the given parity to complete.  Returns
-// false if it did not within FB_WAIT_LIMIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// false if it did not within `limit_ns` nanoseconds.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity))
-        if (globaltimer_ns() - t0 > FB_WAIT_LIMIT_NS) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     return true;
+}
+
+// The bounded wait every kernel uses: FB_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, FB_WAIT_LIMIT_NS);
 }
 
 // Bulk (non-tensor) copy global -> shared, completing on `bar` with `bytes`

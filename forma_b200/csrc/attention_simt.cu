@@ -231,12 +231,12 @@ int launch_attention_decode(const AttnArgs& a, void* stream) {
             break;
         default: return FB_ERR_DTYPE;
     }
-    count_launch();
+    count_launch("attention_part_kernel");
     if (e != cudaSuccess) return FB_ERR_DRIVER;
     if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
     const unsigned mblocks = (unsigned)std::min<uint64_t>((a.rows + 3) / 4, (uint64_t)sm_count() * 16);
     attention_merge_kernel<<<mblocks, 128, 0, s>>>(a, (uint32_t)parts, ws);
-    count_launch();
+    count_launch("attention_merge_kernel");
     return launch_status("kernel launch");
 }
 
@@ -267,7 +267,7 @@ int launch_attention_simt(const AttnArgs& a, void* stream) {
             break;
         default: return FB_ERR_DTYPE;
     }
-    count_launch();
+    count_launch("attention_simt_kernel");
     if (e != cudaSuccess) return FB_ERR_DRIVER;
     return launch_status("kernel launch");
 }

@@ -773,13 +773,13 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     }
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
     kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
-    count_launch();
+    count_launch(kernel_name("attn_fwd_kernel", {D, (int)a.mask_kind, QT}).c_str());
     if (p.splits > 1) {
         if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
         const uint64_t rows = BH * L;
         const unsigned mgrid = (unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sm_count() * 16);
         attn_merge_kernel<D><<<mgrid, 256, 0, st>>>(p);
-        count_launch();
+        count_launch(kernel_name("attn_merge_kernel", {D}).c_str());
     }
     return launch_status("kernel launch");
 }

@@ -181,7 +181,7 @@ int launch_conv_direct(const ConvArgs& a, void* stream) {
         case FB_F16: conv_direct_kernel<__half><<<g, 256, 0, s>>>(a); break;
         default: return FB_ERR_DTYPE;
     }
-    count_launch();
+    count_launch("conv_direct_kernel");
     return launch_status("kernel launch");
 }
 
@@ -206,7 +206,7 @@ int launch_conv2d_f32_tiled(const ConvArgs& a, void* stream) {
         conv2d_f32_tiled_kernel<3, 3><<<(unsigned)blocks, T_THREADS, 0, s>>>(a);
     else
         conv2d_f32_tiled_kernel<1, 1><<<(unsigned)blocks, T_THREADS, 0, s>>>(a);
-    count_launch();
+    count_launch(k3 ? "conv2d_f32_tiled_kernel<3,3>" : "conv2d_f32_tiled_kernel<1,1>");
     return launch_status("kernel launch");
 }
 

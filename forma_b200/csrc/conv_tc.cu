@@ -812,7 +812,7 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const ConvGemmParams
     const uint32_t tiles = p.m_tiles * p.n_tiles;
     const uint32_t grid = tiles < (uint32_t)sm_count() ? tiles : (uint32_t)sm_count();
     kernel<<<grid, THREADS, C::SMEM, st>>>(ta, tb, p);
-    count_launch();
+    count_launch(kernel_name("conv_gemm_kernel", {BN}).c_str());
     return launch_status("kernel launch");
 }
 
@@ -863,7 +863,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb_half, const ConvGem
     const uint32_t tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
     const uint32_t clusters = tiles < (uint32_t)clusters_max ? tiles : (uint32_t)clusters_max;
     conv_gemm_pair_kernel<BN, EPW><<<2 * clusters, C::THREADS, C::SMEM, st>>>(ta, tb_half, p);
-    count_launch();
+    count_launch(kernel_name("conv_gemm_pair_kernel", {BN, EPW}).c_str());
     return launch_status("kernel launch");
 }
 
@@ -1032,7 +1032,7 @@ int launch_patches(const ConvArgs& a, void* stream) {
                                                             a.in_strides[1], (uint32_t)C, (uint32_t)R, (uint32_t)S,
                                                             (uint32_t)P, (uint32_t)Q, M, static_cast<uint16_t*>(pa));
         }
-        count_launch();
+        count_launch(vec8 ? "patches_vec8_kernel" : "patches_kernel");
         if (cudaGetLastError() != cudaSuccess) return launch_status("patch gather");
     }
     // B operand: [O, C, kh, kw] rows, in place when the weights are stored so.
@@ -1048,7 +1048,7 @@ int launch_patches(const ConvArgs& a, void* stream) {
                                                                a.w_stride_o, a.w_stride_c, a.w_strides[0], a.w_strides[1],
                                                                (uint32_t)O, (uint32_t)C, (uint32_t)R, (uint32_t)S,
                                                                static_cast<uint16_t*>(tmp));
-        count_launch();
+        count_launch("weights_to_oihw_kernel");
         if (cudaGetLastError() != cudaSuccess) return launch_status("weight gather");
         wptr = tmp;
     }
@@ -1132,7 +1132,7 @@ int launch_conv_tc(const ConvArgs& a, void* stream) {
                                                                a.w_stride_o, a.w_stride_c, a.w_strides[0], a.w_strides[1],
                                                                (uint32_t)O, (uint32_t)C, (uint32_t)R, (uint32_t)S,
                                                                static_cast<uint16_t*>(tmp));
-        count_launch();
+        count_launch("weights_to_ohwi_kernel");
         if (cudaGetLastError() != cudaSuccess) return FB_ERR_DRIVER;
         wptr = tmp;
     }

@@ -64,7 +64,7 @@ int launch_gemm_simt(const GemmArgs& g, void* stream) {
     const unsigned gx = (unsigned)(tiles < cap ? tiles : cap);
     const unsigned gy = (unsigned)(g.batch < 65535 ? g.batch : 65535);
     gemm_simt_kernel<<<dim3(gx, gy), dim3(T16, T16), 0, static_cast<cudaStream_t>(stream)>>>(g, n_tiles, tiles);
-    count_launch();
+    count_launch("gemm_simt_kernel");
     return launch_status("gemm");
 }
 

@@ -112,11 +112,14 @@ int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, u
                uint64_t out_off, const Nest& on, uint64_t count, bool dense, void* stream) {
     if (count == 0) return FB_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const char* name = "add_kernel";
     if (dense) {
+        name = "add_dense_kernel";
         add_dense_kernel<<<grid_of(count / 4), BLOCK, 0, st>>>(reinterpret_cast<const float4*>(a + a_off),
                                                               reinterpret_cast<const float4*>(b + b_off),
                                                               reinterpret_cast<float4*>(out + out_off), count / 4);
     } else if (add_vec4_ok(a + a_off, an, b + b_off, bn, out + out_off, on)) {
+        name = "add_vec4_kernel";
         if (count < (1ull << 32))
             add_vec4_kernel<uint32_t><<<grid_of(count / 4), BLOCK, 0, st>>>(a + a_off, an, b + b_off, bn, out + out_off, on,
                                                                            (uint32_t)(count / 4));
@@ -126,7 +129,7 @@ int launch_add(const float* a, uint64_t a_off, const Nest& an, const float* b, u
     } else {
         add_kernel<<<grid_of(count), BLOCK, 0, st>>>(a, a_off, an, b, b_off, bn, out, out_off, on, count);
     }
-    count_launch();
+    count_launch(name);
     return launch_status("add");
 }
 
@@ -141,7 +144,7 @@ int launch_gelu_to_low(const float* in, uint64_t in_off, const Nest& n, uint16_t
         gelu_to_low_kernel<<<grid_of(count), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(in, in_off, n, out, dtype,
                                                                                             count);
     }
-    count_launch();
+    count_launch(vec8_ok(n, in, in_off, out) ? "gelu_to_low_vec8_kernel" : "gelu_to_low_kernel");
     return launch_status("gelu");
 }
 

@@ -4,6 +4,8 @@
 #pragma once
 
 #include <cstdint>
+#include <initializer_list>
+#include <string>
 
 #include "../../include/forma_b200.h"
 
@@ -82,11 +84,23 @@ enum ScratchSlot : int {
     SCRATCH_STATS = 4,        // f32 statistics result before low rounding
     SCRATCH_ATTN_SPLIT = 5,   // split-key attention partials (f64 per row and key range)
     SCRATCH_ATTN_RESULT = 6,  // f32 attention result before low rounding
-    SCRATCH_SLOTS = 7,
+    SCRATCH_COLLECTIVE = 7,   // the global sum's f64 partial, all-reduced in place
+    SCRATCH_SLOTS = 8,
 };
 void* scratch(void* stream, uint64_t bytes, int slot);
 int sm_count();
-void count_launch();
+// Records one enqueued launch of `kernel`: counted by fb_launch_count and
+// appended to this host thread's fb_last_route.
+void count_launch(const char* kernel);
+// "base<p0,p1,...>": the name of a template instantiation for count_launch.
+std::string kernel_name(const char* base, std::initializer_list<int> params);
+// Starts a new route record for this host thread (every entry point calls it).
+void begin_route();
+// Launches this host thread has enqueued (prepared programs count theirs).
+uint64_t thread_launch_count();
+// In-place NCCL sum of `count` doubles on `stream` (collective.cpp); the
+// communicator must belong to the current device.
+int nccl_all_reduce_sum_f64(double* buf, uint64_t count, void* comm, void* stream);
 // Records the pending CUDA error (if any) with `what` as this thread's driver
 // error detail and returns FB_OK when there was none, FB_ERR_DRIVER otherwise.
 int launch_status(const char* what);
@@ -105,6 +119,9 @@ int launch_finish_sum(const double* partial, float* out, void* stream);
 // The no-allocation variant: scratch in a static device array (reduce.cu).
 int launch_sum_partial_static(const Rows& in, double* partial, void* stream);
 uint64_t static_sum_max_elements();
+// One CTA whose bounded wait on an mbarrier nobody arrives at gives up after
+// `limit_ns` and records DEV_SELFTEST_TIMEOUT (fb_selftest_bounded_wait).
+int launch_selftest_wait(uint64_t limit_ns, void* stream);
 // Writes `count` elements of `value` (f32 or u32 bits) into a dense-permuted output.
 int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream);
 // Copies a strided view into a (dense-permuted) output of the same logical shape.

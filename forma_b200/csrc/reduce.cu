@@ -14,6 +14,7 @@
 // argmax compare total-order keys so they are exact and order-independent.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -965,8 +966,8 @@ unsigned grid_for(uint64_t work, unsigned per_sm = 8) {
     return (unsigned)(g ? g : 1);
 }
 
-int check_launch() {
-    count_launch();
+int check_launch(const char* kernel) {
+    count_launch(kernel);
     return launch_status("kernel launch");
 }
 
@@ -984,7 +985,7 @@ int reduce_typed(uint32_t op, const Rows& in, const RowOut& out, cudaStream_t s)
         reduce_rows_kernel<T, 4><<<g, BLOCK, 0, s>>>(in, out, op);
     else
         reduce_rows_kernel<T, 1><<<g, BLOCK, 0, s>>>(in, out, op);
-    return check_launch();
+    return check_launch("reduce_rows_kernel");
 }
 
 template <typename T>
@@ -1007,7 +1008,7 @@ int stats_typed(uint32_t op, const Rows& in, const ElemOut& out, const RowOut& a
         stats_rows_kernel<T, 8><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
     else
         stats_rows_kernel<T, 0><<<g, BLOCK, 0, s>>>(in, out, a, b, op, eps);
-    return check_launch();
+    return check_launch("stats_rows_kernel");
 }
 
 // Launches the streamed engine when the geometry allows it; returns
@@ -1040,7 +1041,7 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
             const uint64_t want = (in.rows + WARP_ROWS_TB / 32 - 1) / (WARP_ROWS_TB / 32);
             const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
             kernel<<<(unsigned)(want < cap ? want : cap), WARP_ROWS_TB, 0, st>>>(in, op, a, b, eo, eps);
-            return check_launch();
+            return check_launch("rows_warp_kernel");
         };
         auto by_nv = [&](auto fam_c) -> int {
             constexpr int F = decltype(fam_c)::value;
@@ -1078,7 +1079,7 @@ int stream_typed(uint32_t op, const Rows& in, const RowOut& a, const RowOut& b, 
         const uint64_t cap = (uint64_t)sm_count() * (uint64_t)per_sm;
         const unsigned grid = (unsigned)(in.rows < cap ? in.rows : cap);
         kernel<<<grid, threads, smem, st>>>(in, op, a, b, eo, eps, stages, (uint32_t)row_bytes);
-        return check_launch();
+        return check_launch("rows_stream_kernel");
     };
     const bool cap = op == ROW_ARGMAX || op == STREAM_STATS + STATS_MOMENTS;
     const int fam = op == ROW_SUM || op == ROW_MEAN                             ? FAM_SUM
@@ -1150,7 +1151,7 @@ int launch_reduce_rows(uint32_t op, const Rows& in, const RowOut& out, void* str
         case FB_F16: return reduce_typed<__half>(op, in, out, s);
         case FB_U32:
             reduce_rows_u32_kernel<<<grid_for(in.rows), BLOCK, 0, s>>>(in, out, op);
-            return check_launch();
+            return check_launch("reduce_rows_u32_kernel");
         default: return FB_ERR_DTYPE;
     }
 }
@@ -1194,7 +1195,7 @@ int launch_sum_partial(const Rows& in, double* partial, void* stream) {
         sum_stream_kernel<<<g, kSumTB, smem, s>>>(base, chunks, in.cols % kSumChunk, stages,
                                                    reinterpret_cast<double*>(scr + 256),
                                                    reinterpret_cast<unsigned*>(scr), partial);
-        return check_launch();
+        return check_launch("sum_stream_kernel");
     }
     const unsigned g = (unsigned)sm_count() * 4;
     char* scr = static_cast<char*>(scratch(stream, 256 + (uint64_t)g * sizeof(double), SCRATCH_SUM));
@@ -1205,7 +1206,7 @@ int launch_sum_partial(const Rows& in, double* partial, void* stream) {
         sum_partial_kernel<4><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
     else
         sum_partial_kernel<1><<<g, BLOCK, 0, s>>>(in, partials, counter, partial);
-    return check_launch();
+    return check_launch("sum_partial_kernel");
 }
 
 // Global-sum partial without allocation.  Some callers cannot call
@@ -1250,8 +1251,13 @@ uint64_t static_sum_max_elements() { return kStaticPartials * kStaticBlockElems;
 
 int launch_sum_partial_static(const Rows& in, double* partial, void* stream) {
     const uint64_t count = in.cols;
-    const uint64_t blocks = count == 0 ? 1 : (count + kStaticBlockElems - 1) / kStaticBlockElems;
-    if (blocks > kStaticPartials) return FB_ERR_INVALID_INPUT;
+    const uint64_t needed = count == 0 ? 1 : (count + kStaticBlockElems - 1) / kStaticBlockElems;
+    if (needed > kStaticPartials) return FB_ERR_INVALID_INPUT;
+    // The kernel is grid-stride: at least four blocks per SM (as the
+    // allocating path launches) so small inputs get the full bandwidth, one
+    // per 2^18 elements beyond that, never more partials than the array holds.
+    const uint64_t floor_blocks = std::min<uint64_t>((uint64_t)sm_count() * 4, kStaticPartials);
+    const uint64_t blocks = std::max(needed, floor_blocks);
     void* base = nullptr;
     const int rc = static_sum_scratch(&base);
     if (rc != FB_OK) return rc;
@@ -1264,19 +1270,36 @@ int launch_sum_partial_static(const Rows& in, double* partial, void* stream) {
         sum_partial_kernel<4><<<(unsigned)blocks, BLOCK, 0, s>>>(in, partials, counter, partial);
     else
         sum_partial_kernel<1><<<(unsigned)blocks, BLOCK, 0, s>>>(in, partials, counter, partial);
-    return check_launch();
+    return check_launch("sum_partial_kernel");
+}
+
+// One thread waits on an mbarrier that nothing arrives at, with the same
+// bounded wait every kernel here uses but a caller-chosen limit; the wait
+// gives up, the timeout is recorded in the status word and the kernel
+// returns.  No copy or MMA is in flight, so nothing needs draining.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    if (!mbar_wait_for(&bar, 0, limit_ns)) atomicOr(&g_reduce_status, 1u << DEV_SELFTEST_TIMEOUT);
+}
+
+int launch_selftest_wait(uint64_t limit_ns, void* stream) {
+    selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns);
+    return check_launch("selftest_wait_kernel");
 }
 
 int launch_finish_sum(const double* partial, float* out, void* stream) {
     finish_sum_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(partial, out);
-    return check_launch();
+    return check_launch("finish_sum_kernel");
 }
 
 int launch_fill(void* data, uint64_t count, uint32_t bits, void* stream) {
     if (count == 0) return FB_OK;
     fill_kernel<<<grid_for((count + BLOCK - 1) / BLOCK), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<uint32_t*>(data), count, bits);
-    return check_launch();
+    return check_launch("fill_kernel");
 }
 
 int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const Nest& in_nest, void* out,
@@ -1290,7 +1313,7 @@ int launch_copy(const void* in, uint32_t elem_bytes, uint64_t in_offset, const N
     else
         copy_kernel<uint16_t><<<g, BLOCK, 0, s>>>(static_cast<const uint16_t*>(in), in_offset, in_nest,
                                                   static_cast<uint16_t*>(out), out_offset, out_nest, count);
-    return check_launch();
+    return check_launch("copy_kernel");
 }
 
 int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest, uint16_t* out, uint32_t dtype,
@@ -1300,11 +1323,11 @@ int launch_cast_to_low(const float* in, uint64_t in_offset, const Nest& in_nest,
         const uint64_t runs = count / 8;
         cast_to_low_vec8_kernel<<<grid_for((runs + BLOCK - 1) / BLOCK, 16), BLOCK, 0,
                                   static_cast<cudaStream_t>(stream)>>>(in, in_offset, in_nest, out, dtype, runs);
-        return check_launch();
+        return check_launch("cast_to_low_vec8_kernel");
     }
     cast_to_low_kernel<<<grid_for((count + BLOCK - 1) / BLOCK), BLOCK, 0, static_cast<cudaStream_t>(stream)>>>(
         in, in_offset, in_nest, out, dtype, count);
-    return check_launch();
+    return check_launch("cast_to_low_kernel");
 }
 
 }  // namespace fb

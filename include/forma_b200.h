@@ -20,6 +20,14 @@
  *    stream) and is asynchronous, like the reference's single-stream runtime
  *    (compute-cuda/src/runtime.rs:66-81).
  *  - There is no CPU fallback: a missing device or kernel is FB_ERR_DRIVER.
+ *  - Every call runs on the calling thread's current device (cudaSetDevice),
+ *    which must own every operand and the stream, as the reference's runtime
+ *    owns one device (compute-cuda/src/runtime.rs:66-81).  Library scratch is
+ *    kept per (device, stream); host threads that call concurrently must use
+ *    different streams or the per-thread default stream (cudaStreamPerThread,
+ *    keyed per thread).  Resetting a device (cudaDeviceReset) invalidates
+ *    every device address the library has cached for it: make no further
+ *    calls on that device in the same process.
  */
 #ifndef FORMA_B200_H
 #define FORMA_B200_H
@@ -67,6 +75,10 @@ typedef enum fb_status {
     FB_ERR_DTYPE = 33,
     FB_ERR_DRIVER = 34,
     FB_ERR_UNSUPPORTED = 35,
+    FB_ERR_FOREIGN_RUNTIME = 36,  /* CudaError::ForeignRuntime: another device's object */
+    FB_ERR_MISSING_SYMBOL = 37,   /* CudaError::MissingSymbol (compute-cuda/src/libraries.rs:100-117) */
+    FB_ERR_GRAPH = 38,            /* CudaError::Graph: recording or instantiating a program failed */
+    FB_ERR_PROGRAM_POISONED = 39, /* CudaError::ProgramPoisoned */
 } fb_status;
 
 /* Strided view of device storage (compute-cuda/src/runtime.rs:44-61:
@@ -129,6 +141,14 @@ const char* fb_status_string(int status);
 const char* fb_last_error(void);
 /* Number of kernel launches this library has enqueued (all threads). */
 uint64_t fb_launch_count(void);
+/* The kernels that the most recent computing call on this host thread
+ * enqueued, comma-separated in launch order, template instantiations
+ * spelled out (e.g. "conv_gemm_pair_kernel<192,8>" or
+ * "attn_fwd_kernel<128,0,2>,attn_merge_kernel<128>"); "" when that call
+ * launched nothing.  Shows which route (tensor cores, CUDA cores, split,
+ * scratch + cast) served a call.  No counterpart in the reference, whose
+ * kernels are fixed per operation.  Valid until the thread's next call. */
+const char* fb_last_route(void);
 /* Synchronises the current device and returns (and clears) a bit mask of
  * bounded waits that timed out inside this library's kernels since the last
  * call (0 = none).  A kernel that gives up a wait writes no partial result
@@ -255,6 +275,35 @@ int fb_sum_partial_f64(const fb_tensor* input, double* partial, void* stream);
  * element, any rank with numel 1). */
 int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream);
 
+/* --------------------------------------------------------- multi-GPU sum */
+
+/* The global sum of rows sharded across GPUs (one process or thread per GPU,
+ * or one process driving several): the f64 partial of this shard, ONE
+ * in-place NCCL all-reduce of 8 bytes over `comm` on `stream`, and the f32
+ * rounding into `output` (one element), all enqueued on the caller's stream.
+ * Every rank of the communicator makes the same call.  The reference runtime
+ * is single-device per process (gpu-compute/src/cuda.rs:80-86), so the
+ * exchange lives in the backend; it replaces the multi-pass reduce_all of
+ * compute-cuda/src/reduction.rs:145-160 at the scale of several GPUs.
+ * `comm` is an ncclComm_t of the current device (FB_ERR_FOREIGN_RUNTIME
+ * otherwise).  NCCL is loaded at run time ($FB_NCCL_LIBRARY, else the copy the
+ * process already loaded, else libnccl.so.2); every symbol is checked before
+ * the first call and a missing one is FB_ERR_MISSING_SYMBOL. */
+int fb_global_sum_nccl(const fb_tensor* shard, void* comm, fb_tensor* output, void* stream);
+
+/* Communicator set-up for fb_global_sum_nccl, so a caller needs no NCCL
+ * bindings of its own.  fb_nccl_unique_id writes FB_NCCL_UNIQUE_ID_BYTES
+ * bytes (rank 0 creates it and hands it to the other ranks);
+ * fb_nccl_comm_init_rank joins rank `rank` of `nranks` on the current
+ * device; fb_nccl_comm_init_all creates one communicator per listed device
+ * in one process (devices NULL = 0..ndev-1); fb_nccl_comm_destroy releases
+ * one (NULL is a no-op). */
+#define FB_NCCL_UNIQUE_ID_BYTES 128
+int fb_nccl_unique_id(void* id);
+int fb_nccl_comm_init_rank(void** comm, int nranks, const void* id, int rank);
+int fb_nccl_comm_init_all(void** comms, int ndev, const int* devices);
+int fb_nccl_comm_destroy(void* comm);
+
 /* Size of the per-device static scratch array of fb_sum_partial_f64_static. */
 #define FB_SUM_STATIC_SCRATCH_BYTES 65536
 
@@ -265,9 +314,11 @@ int fb_finish_sum_f64(const double* partial, fb_tensor* output, void* stream);
  * is not acceptable, cannot let a library call cudaMalloc; this entry point
  * calls no allocating routine.  Its block partials and finishing counter live
  * in a file-scope device array of FB_SUM_STATIC_SCRATCH_BYTES that every GPU
- * loading the library keeps until the process exits.  Limits: one partial
- * per 2^18 input elements, so inputs above fb_sum_static_max_elements()
- * elements (about 2.1e9) are rejected with FB_ERR_INVALID_INPUT.  Every call
+ * loading the library keeps until the process exits.  Limits: each block
+ * leaves one partial in the array; a call launches four blocks per SM, or
+ * one per 2^18 input elements when that is more, so inputs above
+ * fb_sum_static_max_elements() elements (8160 x 2^18, about 2.1e9) are
+ * rejected with FB_ERR_INVALID_INPUT before anything is enqueued.  Every call
  * shares the array (the counter is cleared at the start of each call): calls
  * that overlap on the GPU, on any stream, race.  The first call on each
  * device looks up the array's device address (cached afterwards); make that
@@ -365,6 +416,42 @@ int fb_conv_low_gelu(const fb_tensor* input, const fb_tensor* weight, const fb_c
  * (FB_ERR_INVALID_INPUT). */
 int fb_conv_low_f32_accumulate(const fb_tensor* input, const fb_tensor* weight, const fb_conv_options* options,
                                fb_tensor* output, void* stream);
+
+/* ------------------------------------------------------ prepared programs */
+
+/* A sequence of the calls above recorded once on a stream and replayed as
+ * one CUDA graph launch with the same buffers: the reference's prepared
+ * programs with CUDA Graph capture (compute-cuda/src/program.rs:1-60,
+ * program/graph.rs, program/execution.rs:20-150), for any sequence of this
+ * library's operators, convolution included.  fb_program_begin starts
+ * recording on `stream` (a created stream, not a default stream) for this
+ * host thread; the fb_* calls that follow on that stream are recorded, not
+ * run; fb_program_end stops and instantiates.  Recording allocates nothing:
+ * each operator's library scratch must exist already, so run the sequence
+ * once eagerly on the same stream first (a call that would need new scratch
+ * fails while recording, and the recording then fails as FB_ERR_GRAPH, as
+ * does any allocation or synchronising call made while recording).
+ * fb_program_launch replays it; a failed launch poisons the program
+ * (FB_ERR_PROGRAM_POISONED from then on, like CudaError::ProgramPoisoned).
+ * fb_program_stats reports this library's kernels in the recording, the
+ * graph's node count and whether the program is poisoned. */
+typedef struct fb_program fb_program;
+int fb_program_begin(void* stream);
+int fb_program_end(void* stream, fb_program** program);
+int fb_program_launch(fb_program* program, void* stream);
+int fb_program_stats(const fb_program* program, uint64_t* kernel_launches, uint64_t* graph_nodes, int32_t* poisoned);
+int fb_program_destroy(fb_program* program);
+
+/* ------------------------------------------------------------ diagnostics */
+
+/* Launches one CTA whose thread waits on an mbarrier that nothing arrives at,
+ * through the same bounded wait every kernel here uses, with a limit of
+ * `limit_ns` (0 < limit_ns <= 1e9).  The wait gives up, bit 6 is recorded in
+ * the word fb_device_status() returns, and the kernel exits normally, so a
+ * caller can check - without a hang or a fault - that timed-out waits are
+ * reported.  No counterpart in the reference, whose fault injection is on the
+ * host (compute-cuda/src/libraries.rs:120-174). */
+int fb_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
 #ifdef __cplusplus
 }

@@ -232,7 +232,9 @@ def verify(reference: Path) -> None:
 
 
 def main(argv: list[str]) -> int:
-    reference = Path(argv[1] if len(argv) > 1 else "/root/reference")
+    if len(argv) != 2:
+        raise SystemExit(f"usage: {argv[0]} <path of the reference checkout>")
+    reference = Path(argv[1])
     verify(reference)
     (HERE / "golden.json").write_text(json.dumps({"cases": CASES}, indent=1) + "\n")
     print(f"wrote {len(CASES)} cases to {HERE / 'golden.json'}")

@@ -13,13 +13,16 @@ from oracle import oracle as orc
 pytestmark = pytest.mark.gpu
 
 
-def check(cuda, qs, ks, vs, causal=None, scale=None, dtype=torch.bfloat16, seed=0, vconst=None):
+def check(cuda, qs, ks, vs, causal=None, scale=None, dtype=torch.bfloat16, seed=0, vconst=None, expect=None):
+    """`expect`: the kernels the call must launch (fb_last_route), tcgen05 first."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     q = torch.randn(*qs, generator=g).to(dtype)
     k = torch.randn(*ks, generator=g).to(dtype)
     v = torch.randn(*vs, generator=g).to(dtype) if vconst is None else torch.full(vs, vconst).to(dtype)
     before = api.launch_count()
-    out = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), None, AttentionOptions(scale, causal)).cpu().numpy()
+    out = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), None, AttentionOptions(scale, causal))
+    assert api.last_route() == expect, api.last_route()  # the tensor-core kernel, not a CUDA-core fallback
+    out = out.cpu().numpy()
     assert api.device_status() == 0, "a bounded wait timed out"
     assert api.launch_count() > before
     ref = orc.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), None, scale, causal,
@@ -34,31 +37,35 @@ def check(cuda, qs, ks, vs, causal=None, scale=None, dtype=torch.bfloat16, seed=
 
 
 def test_tc_attention_causal_d128(cuda):
-    check(cuda, (1, 2, 256, 128), (1, 2, 256, 128), (1, 2, 256, 128), causal=0)
+    check(cuda, (1, 2, 256, 128), (1, 2, 256, 128), (1, 2, 256, 128), causal=0, expect=["attn_fwd_kernel<128,0,2>"])
 
 
 def test_tc_attention_ragged_noncausal_d128(cuda):
-    check(cuda, (1, 2, 300, 128), (1, 2, 300, 128), (1, 2, 300, 128))
+    check(cuda, (1, 2, 300, 128), (1, 2, 300, 128), (1, 2, 300, 128), expect=["attn_fwd_kernel<128,0,2>"])
 
 
 def test_tc_attention_vit_shape_d64(cuda):
-    check(cuda, (2, 3, 197, 64), (2, 3, 197, 64), (2, 3, 197, 64))
+    check(cuda, (2, 3, 197, 64), (2, 3, 197, 64), (2, 3, 197, 64), expect=["attn_fwd_kernel<64,0,1>"])
 
 
 def test_tc_attention_gqa_and_offsets(cuda):
     for causal in (-5, 100, -300):
-        out, ref = check(cuda, (1, 4, 256, 64), (1, 2, 256, 64), (1, 2, 256, 64), causal=causal, seed=7)
+        out, ref = check(cuda, (1, 4, 256, 64), (1, 2, 256, 64), (1, 2, 256, 64), causal=causal, seed=7,
+                         expect=["attn_fwd_kernel<64,0,1>"])
         if causal == -300:
             assert (out == 0).all()  # every row fully masked
 
 
 def test_tc_attention_f16_and_scale(cuda):
-    check(cuda, (1, 2, 256, 128), (1, 2, 384, 128), (1, 2, 384, 128), causal=128, scale=0.05, dtype=torch.float16)
+    check(cuda, (1, 2, 256, 128), (1, 2, 384, 128), (1, 2, 384, 128), causal=128, scale=0.05, dtype=torch.float16,
+          expect=["attn_fwd_kernel<128,0,2>"])
 
 
 def test_tc_attention_large_values_do_not_overflow(cuda):
     big = 3.3e38  # near the bf16 maximum: the unnormalised numerator must stay finite
-    out, ref = check(cuda, (1, 1, 128, 64), (1, 1, 4096, 64), (1, 1, 4096, 64), vconst=big)
+    # one CTA's worth of queries over 32 key tiles: the key range is split across CTAs and merged
+    out, ref = check(cuda, (1, 1, 128, 64), (1, 1, 4096, 64), (1, 1, 4096, 64), vconst=big,
+                     expect=["attn_fwd_kernel<64,0,2>", "attn_merge_kernel<64>"])
     assert np.isfinite(out).all()
 
 
@@ -70,6 +77,7 @@ def test_tc_attention_c4_size_sampled(cuda):
     k = torch.randn(8, 32, 4096, 128, device=cuda, generator=g).bfloat16()
     v = torch.randn(8, 32, 4096, 128, device=cuda, generator=g).bfloat16()
     out = api.attention_low_f32(q, k, v, None, AttentionOptions(causal=0))
+    assert api.last_route() == ["attn_fwd_kernel<128,0,2>"], api.last_route()
     assert api.device_status() == 0
     for b, h in ((0, 0), (7, 31)):
         ref = orc.attention(q[b, h].float().cpu().numpy(), k[b, h].float().cpu().numpy(),
@@ -86,6 +94,8 @@ def _check_views(cuda, q, k, v, out=None, causal=None, tol=2e-2):
         got = api.attention_low_f32(q, k, v, None, AttentionOptions(None, causal))
     else:
         got = api.attention_low_f32_into(q, k, v, None, AttentionOptions(None, causal), out)
+    route = api.last_route()
+    assert len(route) == 1 and route[0].startswith(f"attn_fwd_kernel<{q.shape[-1]},0,"), route
     assert api.device_status() == 0
     assert api.launch_count() > before
     ref = orc.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), None, None,
@@ -140,7 +150,11 @@ def _masked_case(cuda, kind, qs, ks, mshape, causal=None, seed=41):
         mask = Mask("additive", add.to(cuda))
         additive = add.numpy().astype(np.float64)
     before = api.launch_count()
-    got = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), mask, AttentionOptions(None, causal)).cpu().numpy()
+    got = api.attention_low_f32(q.to(cuda), k.to(cuda), v.to(cuda), mask, AttentionOptions(None, causal))
+    mk = 1 if kind == "keep" else 2
+    route = api.last_route()
+    assert len(route) == 1 and route[0].startswith(f"attn_fwd_kernel<{qs[-1]},{mk},"), route  # masks on the tensor cores
+    got = got.cpu().numpy()
     assert api.device_status() == 0
     assert api.launch_count() > before
     ref = orc.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), additive, None, causal,

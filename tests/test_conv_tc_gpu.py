@@ -13,7 +13,9 @@ from oracle import oracle as orc
 pytestmark = pytest.mark.gpu
 
 
-def run_case(cuda, n, h, w, c, o, k, stride=1, pad=0, dtype=torch.bfloat16, ohwi=True, nchw_out=True, seed=0):
+def run_case(cuda, n, h, w, c, o, k, stride=1, pad=0, dtype=torch.bfloat16, ohwi=True, nchw_out=True, seed=0,
+             expect=None):
+    """`expect`: the tensor-core GEMM kernel the call must launch (fb_last_route)."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     x = torch.randn(n, h, w, c, generator=g).to(dtype)
     wt = (torch.randn(o, k, k, c, generator=g) * (2.0 / (c * k * k)) ** 0.5).to(dtype)
@@ -30,6 +32,10 @@ def run_case(cuda, n, h, w, c, o, k, stride=1, pad=0, dtype=torch.bfloat16, ohwi
         dims = api.conv_plan(list(xv.shape), list(wv.shape), opts)
         store = torch.empty(dims[0], dims[2], dims[3], dims[1], device=cuda)
         out = api.conv_low_f32_into(xv, wv, opts, store.permute(0, 3, 1, 2))
+    route = api.last_route()
+    assert expect in route, route  # the tensor cores served the call, not a CUDA-core fallback
+    if not ohwi:
+        assert route[0] == "weights_to_ohwi_kernel", route
     got = out.cpu().numpy()
     assert api.device_status() == 0, "a bounded wait timed out"
     assert api.launch_count() > before
@@ -46,34 +52,34 @@ def run_case(cuda, n, h, w, c, o, k, stride=1, pad=0, dtype=torch.bfloat16, ohwi
 
 
 def test_tc_conv_1x1(cuda):
-    run_case(cuda, 4, 14, 14, 1024, 256, 1)
+    run_case(cuda, 4, 14, 14, 1024, 256, 1, expect="conv_gemm_pair_kernel<256,4>")
 
 
 def test_tc_conv_3x3_pad1(cuda):
-    run_case(cuda, 2, 14, 14, 256, 256, 3, pad=1)
+    run_case(cuda, 2, 14, 14, 256, 256, 3, pad=1, expect="conv_gemm_pair_kernel<256,4>")
 
 
 def test_tc_conv_3x3_stride2(cuda):
-    run_case(cuda, 2, 28, 28, 128, 128, 3, stride=2, pad=1)
+    run_case(cuda, 2, 28, 28, 128, 128, 3, stride=2, pad=1, expect="conv_gemm_kernel<128>")
 
 
 def test_tc_conv_partial_tile_and_small_n(cuda):
-    run_case(cuda, 3, 7, 7, 512, 64, 3, pad=1)  # M = 147, BN = 64
+    run_case(cuda, 3, 7, 7, 512, 64, 3, pad=1, expect="conv_gemm_kernel<64>")  # M = 147, BN = 64
 
 
 def test_tc_conv_oihw_weights_and_nhwc_output(cuda):
-    run_case(cuda, 2, 14, 14, 256, 128, 3, pad=1, ohwi=False, nchw_out=False)
+    run_case(cuda, 2, 14, 14, 256, 128, 3, pad=1, ohwi=False, nchw_out=False, expect="conv_gemm_kernel<128>")
 
 
 def test_tc_conv_nhwc_output_partial_tile(cuda):
     # channels-last f32 result through the staged float4 epilogue; M = 189
     # leaves a partial last tile whose missing rows must not be stored
-    run_case(cuda, 3, 7, 9, 64, 64, 1, nchw_out=False)
-    run_case(cuda, 3, 7, 7, 512, 64, 3, pad=1, nchw_out=False)
+    run_case(cuda, 3, 7, 9, 64, 64, 1, nchw_out=False, expect="conv_gemm_kernel<64>")
+    run_case(cuda, 3, 7, 7, 512, 64, 3, pad=1, nchw_out=False, expect="conv_gemm_kernel<64>")
 
 
 def test_tc_conv_f16(cuda):
-    run_case(cuda, 2, 14, 14, 256, 256, 3, pad=1, dtype=torch.float16)
+    run_case(cuda, 2, 14, 14, 256, 256, 3, pad=1, dtype=torch.float16, expect="conv_gemm_pair_kernel<256,4>")
 
 
 def test_tc_conv_c3_shapes_sampled(cuda):
@@ -85,6 +91,7 @@ def test_tc_conv_c3_shapes_sampled(cuda):
         w = (torch.randn(256, k, k, c, device=cuda, generator=g) * (2.0 / (c * k * k)) ** 0.5).bfloat16()
         opts = ConvOptions([1, 1], [1, 1], [pad, pad], [pad, pad])
         out = api.conv_low_f32(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2), opts)
+        assert api.last_route() == ["conv_gemm_pair_kernel<256,4>"], api.last_route()
         assert api.device_status() == 0
         for img in (0, 37, 131, 200, 255):
             ref = orc.conv(x[img:img + 1].permute(0, 3, 1, 2).float().cpu().numpy(),
@@ -110,6 +117,7 @@ def test_tc_conv_low_rounds_in_the_epilogue(cuda, dtype, channels_last_out):
         got = api.conv_low_into(x, w, o, store.permute(0, 3, 1, 2))
     else:
         got = api.conv_low(x, w, o)
+    assert api.last_route() == ["conv_gemm_kernel<128>"], api.last_route()  # rounded in the epilogue
     assert api.device_status() == 0
     assert torch.equal(got.contiguous().view(torch.int16).cpu(), ref.contiguous().view(torch.int16).cpu())
 
@@ -121,4 +129,5 @@ def test_patch_conv_low_rounds_in_the_epilogue(cuda):
     o = ConvOptions([16, 16], [1, 1], [0, 0], [0, 0])
     ref = api.cast_to_low(api.conv_low_f32(x, w, o), torch.bfloat16)
     got = api.conv_low(x, w, o)
+    assert api.last_route() == ["patches_vec8_kernel", "conv_gemm_kernel<128>"], api.last_route()
     assert torch.equal(got.view(torch.int16).cpu(), ref.view(torch.int16).cpu())

@@ -16,8 +16,11 @@ def f64(t):
     return t.float().cpu().numpy().astype(np.float64)
 
 
-def check(left, right, tol=2e-2):
+def check(left, right, tol=2e-2, expect=None):
+    """`expect`: the GEMM kernel the call must launch (fb_last_route)."""
     got = api.matmul_low_f32(left, right)
+    if expect is not None:
+        assert expect in api.last_route(), api.last_route()
     assert api.device_status() == 0
     ref = np.matmul(f64(left), f64(right))
     g = got.cpu().numpy().astype(np.float64)
@@ -36,22 +39,24 @@ def rnd(*shape, seed=0, dtype=torch.bfloat16):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_matmul_tensor_core_row_major_right(cuda, dtype):
-    check(rnd(300, 256, seed=1, dtype=dtype).to(cuda), rnd(256, 192, seed=2, dtype=dtype).to(cuda))
+    # N = 192 with a row-major (MN-major) right operand: single-CTA tiles of 64 columns
+    check(rnd(300, 256, seed=1, dtype=dtype).to(cuda), rnd(256, 192, seed=2, dtype=dtype).to(cuda),
+          expect="conv_gemm_kernel<64>")
 
 
 def test_matmul_tensor_core_transposed_right(cuda):
     w = rnd(512, 128, seed=3).to(cuda)  # [N, K] storage
-    check(rnd(200, 128, seed=4).to(cuda), w.t())
+    check(rnd(200, 128, seed=4).to(cuda), w.t(), expect="conv_gemm_pair_kernel<256,4>")
 
 
 def test_matmul_broadcast_batches(cuda):
-    check(rnd(2, 3, 130, 64, seed=5).to(cuda), rnd(3, 64, 128, seed=6).to(cuda))
+    check(rnd(2, 3, 130, 64, seed=5).to(cuda), rnd(3, 64, 128, seed=6).to(cuda), expect="conv_gemm_kernel<128>")
     check(rnd(4, 1, 70, 64, seed=7).to(cuda), rnd(1, 2, 64, 256, seed=8).to(cuda))
 
 
 def test_matmul_vectors_and_odd_shapes(cuda):
     k = rnd(37, 50, seed=9).to(cuda)
-    check(k, rnd(50, 23, seed=10).to(cuda))            # CUDA-core kernel
+    check(k, rnd(50, 23, seed=10).to(cuda), expect="gemm_simt_kernel")  # CUDA-core kernel
     check(rnd(50, seed=11).to(cuda), rnd(50, 23, seed=12).to(cuda))    # [K] x [K, N] -> [N]
     check(k, rnd(50, seed=13).to(cuda))                # [M, K] x [K] -> [M]
     got = api.matmul_low_f32(rnd(64, seed=14).to(cuda), rnd(64, seed=15).to(cuda))
