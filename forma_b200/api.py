@@ -651,4 +651,4 @@ def last_route() -> list:
     """Kernels the most recent call on this thread enqueued, in launch order
     (e.g. ``["conv_gemm_pair_kernel<192,8>"]``)."""
     r = lib().fb_last_route().decode()
-    return r.split(",") if r else []
+    return r.split(";") if r else []

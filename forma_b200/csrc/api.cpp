@@ -27,7 +27,7 @@ namespace {
 std::atomic<uint64_t> g_launches{0};
 thread_local std::string g_driver_error;
 // Kernels enqueued by the current (or most recent) entry-point call of this
-// host thread, comma-separated in launch order.
+// host thread, ';'-separated in launch order.
 thread_local std::string g_route;
 thread_local uint64_t g_thread_launches = 0;
 
@@ -708,7 +708,7 @@ int sm_count() {
 void count_launch(const char* kernel) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
     ++g_thread_launches;
-    if (!g_route.empty()) g_route += ',';
+    if (!g_route.empty()) g_route += ';';
     g_route += kernel;
 }
 

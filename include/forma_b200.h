@@ -142,9 +142,9 @@ const char* fb_last_error(void);
 /* Number of kernel launches this library has enqueued (all threads). */
 uint64_t fb_launch_count(void);
 /* The kernels that the most recent computing call on this host thread
- * enqueued, comma-separated in launch order, template instantiations
+ * enqueued, separated by ';' in launch order, template instantiations
  * spelled out (e.g. "conv_gemm_pair_kernel<192,8>" or
- * "attn_fwd_kernel<128,0,2>,attn_merge_kernel<128>"); "" when that call
+ * "attn_fwd_kernel<128,0,2>;attn_merge_kernel<128>"); "" when that call
  * launched nothing.  Shows which route (tensor cores, CUDA cores, split,
  * scratch + cast) served a call.  No counterpart in the reference, whose
  * kernels are fixed per operation.  Valid until the thread's next call. */
