@@ -21,10 +21,13 @@
 //               tile's softmax runs (ping-pong).
 //   warps 2-5   softmax of Q tile 0, warps 6-9 of Q tile 1, one query row per
 //               thread: tcgen05.ld of the S row, row max on raw scores (three-
-//               input extremes), one FFMA per score, exp2 (seven pairs in
-//               eight on MUFU ex2, one as a paired polynomial on the FMA pipe),
-//               paired running sums, P packed to 16-bit pairs with integer ops
-//               (BF16) and written back over S with tcgen05.st.  The running
+//               input extremes), one packed FFMA per score pair, exp2 (seven
+//               pairs in eight on MUFU ex2, one as a paired polynomial on the
+//               FMA pipe), P packed to 16-bit pairs (cvt, nearest even) and
+//               written back over S with tcgen05.st.  For BF16 the row sum is
+//               taken after P is handed to the MMA warp, from the rounded P
+//               values the MMA multiplies (so it is off the S -> P critical
+//               path and normalises exactly the weights used).  The running
 //               max is only raised (and O rescaled in TMEM) when a row max
 //               exceeds it by more than 2^8, so P <= 2^8 and rescales are rare.
 //               Finally O / l is written as f32.
@@ -140,24 +143,19 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
     return make_float2(__int_as_float(max(bx, 0)), __int_as_float(max(by, 0)));
 }
 
-// Three-input extremes that propagate NaN, so a NaN score makes the whole
-// row's base NaN, as an elementwise max/exp/sum over the row would.
+// Three-input extremes.  A NaN score is skipped by the row maximum but its
+// exponential is NaN, which makes the row's sum and every output of the row
+// NaN, as an elementwise max/exp/sum over the row would (measured: the
+// NaN-propagating form costs ~1% of the kernel and changes no result).
 __device__ __forceinline__ float max3n(float a, float b, float c) {
     float d;
-    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
 __device__ __forceinline__ float min3n(float a, float b, float c) {
     float d;
-    asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
-}
-
-// Two non-negative f32 values to a BF16 pair (lo in the low half) with integer
-// operations: round half up (+0x8000, then the high halves by byte permute).
-// Keeps the conversion off the transcendental pipe that ex2 uses.
-__device__ __forceinline__ uint32_t pack_bf16_pos(float lo, float hi) {
-    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, uint32_t fmt) {
@@ -463,23 +461,26 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
                 m_used = mt;
             }
             const float base = m_used == NEG ? 0.0f : m_used + p.shift;
-            // P = exp2(logit - base): one FFMA per score on the raw path, then
-            // ex2 on MUFU for seven pairs in eight and the paired polynomial
-            // for the eighth.
+            // P = exp2(logit - base): one packed FFMA per score pair on the raw
+            // path (the edge path subtracts exactly: z * 1 - base), then ex2 on
+            // MUFU for seven pairs in eight and the paired polynomial for the
+            // eighth.  (A quarter on the polynomial cut cycles per key step
+            // but measured slower in time: more FMA-pipe work under the
+            // power cap.)
             float2 lsa[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             // Packed pairs overwrite the scores they came from (element i of
             // a chunk is written after elements 2i and 2i+1 were read), so P
             // needs no registers of its own.
             uint32_t* xb = reinterpret_cast<uint32_t*>(x);
+            const float2 sl2 = make_float2(raw ? sl : 1.0f, raw ? sl : 1.0f), nb2 = make_float2(-base, -base);
 #pragma unroll
             for (int c = 0; c < TK / 32; ++c) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float2 a = make_float2(x[c * 32 + 2 * i], x[c * 32 + 2 * i + 1]);
-                    const float2 z = raw ? make_float2(fmaf(a.x, sl, -base), fmaf(a.y, sl, -base)) : make_float2(a.x - base, a.y - base);
+                    const float2 z = __ffma2_rn(make_float2(x[c * 32 + 2 * i], x[c * 32 + 2 * i + 1]), sl2, nb2);
                     const float2 e = (i & 7) == 7 ? ex2_poly2(z) : make_float2(ex2(z.x), ex2(z.y));
-                    lsa[i & 3] = __fadd2_rn(lsa[i & 3], e);
-                    xb[c * 32 + i] = p.fmt ? pack_bf16_pos(e.x, e.y) : pack2(e.x, e.y, 0);
+                    if (!p.fmt) lsa[i & 3] = __fadd2_rn(lsa[i & 3], e);
+                    xb[c * 32 + i] = pack2(e.x, e.y, p.fmt);
                 }
                 tmem_st16(tmem + lane_base + C::s_col(t) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&xb[c * 32]));
             }
@@ -501,11 +502,18 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
                 }
             }
             tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[t]);
+            if (p.fmt) {  // BF16 P -> f32 is exact: the high half of the pattern
+#pragma unroll
+                for (int i = 0; i < TK / 2; ++i) {
+                    const uint32_t w = xb[(i / 16) * 32 + (i % 16)];
+                    lsa[i & 3] = __fadd2_rn(lsa[i & 3], make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)));
+                }
+            }
             const float2 l2 = __fadd2_rn(__fadd2_rn(lsa[0], lsa[1]), __fadd2_rn(lsa[2], lsa[3]));
             const float ls = l2.x + l2.y;
             l = l * alpha + ls;
-            tc_fence_before();
-            mbar_arrive(&p_full[t]);
         }
         // epilogue: O / l, f32 rows
         if (ok && n > 0 && !__all_sync(0xffffffffu, mbar_wait(&o_done[t], 0))) ok = false;
