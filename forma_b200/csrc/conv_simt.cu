@@ -73,12 +73,15 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(ConvArgs a) {
 }
 
 // Tiled 2-D f32 convolution, stride 1, dilation 1, KHxKW taps, dense NCHW
-// input and output and dense OIHW weights.  A 128-thread block computes 32
-// output channels x 4 rows x 32 columns; each thread owns 4 channels x 8
-// consecutive columns of one row (32 accumulators).  Input channels are staged
-// through shared memory 8 at a time with their zero halo.
-constexpr int T_OC = 32, T_ROWS = 4, T_COLS = 32, T_CCH = 8, T_TO = 4, T_TP = 8;
-constexpr int T_THREADS = (T_OC / T_TO) * T_ROWS * (T_COLS / T_TP);  // 128
+// input and output and dense OIHW weights.  A 64-thread block computes 16
+// output channels x 4 rows x 28 columns; each thread owns 4 channels x 7
+// consecutive columns of one row (28 accumulators).  Input channels are staged
+// through shared memory 16 at a time with their zero halo.  (At the C1
+// geometry, 56 x 56 outputs: 896 blocks, six or seven per SM, no padded
+// columns; the 128-thread 32 x 4 x 32 tiling left 12.5% of its columns idle
+// and 4 vs 3 blocks per SM.)
+constexpr int T_OC = 16, T_ROWS = 4, T_COLS = 28, T_CCH = 16, T_TO = 4, T_TP = 7;
+constexpr int T_THREADS = (T_OC / T_TO) * T_ROWS * (T_COLS / T_TP);  // 64
 
 template <int KH, int KW>
 __global__ void __launch_bounds__(T_THREADS) conv2d_f32_tiled_kernel(ConvArgs a) {

@@ -166,3 +166,36 @@ def test_statistics_oracle_huge_offsets_finite():
         # Layer norm stays usable even when the reported variance overflows
         # (conformance/statistics.rs:412-430); log-probabilities may overflow.
         assert np.isfinite(st["norm"]).all() and np.isfinite(st["mean"]).all()
+
+
+def test_reference_kernel_metadata_matches_the_references_own_unit_tests():
+    """The second oracle's restated descriptors against the values the
+    reference's own unit tests assert (compute-cuda/src/convolution.rs:171-189,
+    reduction/dispatch.rs:195-199), and the attention descriptor's bounds."""
+    from oracle import ref_kernels as ref
+
+    meta, out_sp = ref.conv_metadata([2, 4, 5, 7], [140, 35, 7, 1], 11, [6, 2, 2, 3], [12, 6, 3, 1], 3,
+                                     [2, 1], [1, 2], [1, 2], [0, 1], groups=2)
+    assert out_sp == [3, 6]
+    assert meta[:11] == [2, 2, 3, 6, 11, 3, 140, 35, 12, 6, 6]
+    assert meta[11:] == [5, 7, 3, 6, 2, 3, 7, 1, 3, 1, 2, 1, 1, 2, 1, 2]
+    assert ref.reduce_metadata([3, 5, 2], [1, 0, 3], [2, 0]) == [5, 0, 2, 3, 3, 1]
+    # attention: every Q/K/V address the kernel forms stays inside the views
+    q_shape, q_str, k_str, v_str = [2, 4, 70, 48], [13440, 3360, 48, 1], [8640, 4320, 48, 1], [5940, 2970, 33, 1]
+    m = ref.attention_metadata(q_shape, q_str, 0, k_str, 0, v_str, 0, 2)
+    rank, tail = 3, m[15:]
+    dims = m[:3]
+
+    def base(row, strides, offset, group):
+        for d in (2, 1, 0):
+            c = row % dims[d]
+            row //= dims[d]
+            if d == rank - 2:
+                c //= group
+            offset += c * strides[d]
+        return offset
+
+    rows = 2 * 4 * 70
+    assert max(base(r, m[3:6], tail[0], 1) for r in range(rows)) + 47 * tail[4] < 2 * 4 * 70 * 48
+    assert max(base(r, m[6:9], tail[1], tail[10]) for r in range(rows)) + 89 * tail[5] + 47 * tail[6] < 2 * 2 * 90 * 48
+    assert max(base(r, m[9:12], tail[2], tail[10]) for r in range(rows)) + 89 * tail[7] + 32 * tail[8] < 2 * 2 * 90 * 33
