@@ -192,6 +192,19 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// TMA tensor store shared -> global through a 4-D map (bulk-group
+// completion); rows outside the map's extents are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z, int32_t w,
+                                             const void* src) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // im2col load of a 4-D NHWC tensor: `pixels_per_column` consecutive output
 // pixels starting at base pixel (w, h, n), each shifted by the filter tap
 // (off_w, off_h), channels [c, c + channels_per_pixel).

@@ -45,13 +45,14 @@ def test_tc_attention_ragged_noncausal_d128(cuda):
 
 
 def test_tc_attention_vit_shape_d64(cuda):
-    check(cuda, (2, 3, 197, 64), (2, 3, 197, 64), (2, 3, 197, 64), expect=["attn_fwd_kernel<64,0,1>"])
+    # keys fit one TMEM row: one S group over all of them, a single exact-maximum softmax pass
+    check(cuda, (2, 3, 197, 64), (2, 3, 197, 64), (2, 3, 197, 64), expect=["attn_short_kernel"])
 
 
 def test_tc_attention_gqa_and_offsets(cuda):
     for causal in (-5, 100, -300):
         out, ref = check(cuda, (1, 4, 256, 64), (1, 2, 256, 64), (1, 2, 256, 64), causal=causal, seed=7,
-                         expect=["attn_fwd_kernel<64,0,1>"])
+                         expect=["attn_short_kernel"])
         if causal == -300:
             assert (out == 0).all()  # every row fully masked
 
@@ -95,7 +96,8 @@ def _check_views(cuda, q, k, v, out=None, causal=None, tol=2e-2):
     else:
         got = api.attention_low_f32_into(q, k, v, None, AttentionOptions(None, causal), out)
     route = api.last_route()
-    assert len(route) == 1 and route[0].startswith(f"attn_fwd_kernel<{q.shape[-1]},0,"), route
+    assert len(route) == 1 and (route[0].startswith(f"attn_fwd_kernel<{q.shape[-1]},0,") or
+                                route[0] == "attn_short_kernel"), route
     assert api.device_status() == 0
     assert api.launch_count() > before
     ref = orc.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), None, None,
@@ -174,3 +176,30 @@ def test_tc_attention_keep_mask_broadcast(cuda):
 def test_tc_attention_additive_mask_per_head_causal(cuda):
     # additive mask with -inf entries, per head (broadcast over batch), causal, D = 128
     _masked_case(cuda, "additive", (2, 2, 256, 128), (2, 2, 256, 128), (1, 2, 256, 256), causal=0)
+
+
+@pytest.mark.parametrize("case", ["ragged_129", "one_key", "full_256", "causal_masked_rows", "f16_negative_scale",
+                                  "gqa_packed_decode", "large_values"])
+def test_short_key_range_kernel(cuda, case):
+    """Key ranges of at most 256 at depth 64 (attn_short_kernel): key counts
+    that are not multiples of the MMA step, a single key, a full 256-key row,
+    causal offsets that mask whole rows, f16 with a negative scale, grouped
+    decode rows packed into one tile (query index = row mod L), and values
+    near the BF16 maximum (the numerator's pre-scale)."""
+    kw = dict(expect=["attn_short_kernel"])
+    if case == "ragged_129":
+        check(cuda, (2, 2, 150, 64), (2, 2, 129, 64), (2, 2, 129, 64), **kw)
+    elif case == "one_key":
+        check(cuda, (1, 2, 70, 64), (1, 2, 1, 64), (1, 2, 1, 64), **kw)
+    elif case == "full_256":
+        check(cuda, (1, 2, 256, 64), (1, 2, 256, 64), (1, 2, 256, 64), causal=0, **kw)
+    elif case == "causal_masked_rows":
+        out, ref = check(cuda, (1, 2, 200, 64), (1, 2, 180, 64), (1, 2, 180, 64), causal=-40, **kw)
+        assert (out[:, :, :40] == 0).all()  # rows whose visible keys start past the range
+    elif case == "f16_negative_scale":
+        check(cuda, (1, 3, 100, 64), (1, 3, 222, 64), (1, 3, 222, 64), scale=-0.09, dtype=torch.float16, **kw)
+    elif case == "gqa_packed_decode":
+        check(cuda, (2, 8, 3, 64), (2, 2, 200, 64), (2, 2, 200, 64), causal=150, **kw)
+    else:
+        out, ref = check(cuda, (1, 1, 128, 64), (1, 1, 250, 64), (1, 1, 250, 64), vconst=3.3e38, **kw)
+        assert np.isfinite(out).all()

@@ -89,7 +89,7 @@ def test_c5_forward_at_configured_size_matches_oracle(cuda):
 def test_c5_layer_kernels_are_the_tensor_core_ones(cuda):
     """Every contraction of one encoder forward at batch 64 runs on tcgen05:
     the route of each call (patch gather + GEMM, QKV / fc1 / residual pair
-    GEMMs, one-Q-tile attention) recorded through fb_last_route."""
+    GEMMs, the short-range attention kernel) recorded through fb_last_route."""
     cfg = ViTConfig()
     enc = ViTEncoder(cfg, cuda, seed=1)
     img = torch.randn(cfg.batch, 3, 224, 224, generator=torch.Generator(device="cpu").manual_seed(3)).bfloat16()
@@ -108,8 +108,8 @@ def test_c5_layer_kernels_are_the_tensor_core_ones(cuda):
     assert api.device_status() == 0
     kinds = {r for route in seen for r in route}
     assert "conv_gemm_pair_kernel<192,8>" in kinds  # QKV, fc1, proj, fc2
-    assert "attn_fwd_kernel<64,0,1>" in kinds
+    assert "attn_short_kernel" in kinds
     assert "patches_vec8_kernel" in kinds and "rows_warp_kernel" in kinds
     simt = {"conv_direct_kernel", "attention_simt_kernel", "attention_part_kernel", "gemm_simt_kernel"}
     assert not (kinds & simt), kinds & simt
-    assert sum(1 for route in seen if "attn_fwd_kernel<64,0,1>" in route) == cfg.layers
+    assert sum(1 for route in seen if "attn_short_kernel" in route) == cfg.layers
