@@ -567,7 +567,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN_, EPW>::T
                         for (int j = 0; j < 16; ++j)
                             w[j] = encode_low_pair(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]), p.out_low);
                         uint16_t* dst = out16 + base + c0;
-                        if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                        if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+                            // 32-byte stores: one full sector per instruction
+#pragma unroll
+                            for (int q = 0; q < 2; ++q)
+                                asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst + 16 * q),
+                                             "r"(w[8 * q]), "r"(w[8 * q + 1]), "r"(w[8 * q + 2]), "r"(w[8 * q + 3]),
+                                             "r"(w[8 * q + 4]), "r"(w[8 * q + 5]), "r"(w[8 * q + 6]), "r"(w[8 * q + 7])
+                                             : "memory");
+                        } else if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q)
                                 reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);

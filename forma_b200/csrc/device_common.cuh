@@ -94,9 +94,17 @@ __device__ __forceinline__ uint16_t encode_bf16(float value) {
     return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
 }
 __device__ __forceinline__ uint16_t encode_f16(float value) { return __half_as_ushort(__float2half_rn(value)); }
+// Two values to a 16-bit pair (lo in the low half).  BF16: one nearest-even
+// cvt for both (the same rounding as encode_bf16 for every non-NaN value,
+// subnormals included); a NaN keeps encode_bf16's result (payload high bits,
+// quiet bit set) instead of the cvt's canonical NaN.
 __device__ __forceinline__ uint32_t encode_low_pair(float lo, float hi, uint32_t dtype) {
-    return dtype == FB_BF16 ? (uint32_t)encode_bf16(lo) | ((uint32_t)encode_bf16(hi) << 16)
-                            : (uint32_t)encode_f16(lo) | ((uint32_t)encode_f16(hi) << 16);
+    if (dtype != FB_BF16) return (uint32_t)encode_f16(lo) | ((uint32_t)encode_f16(hi) << 16);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    if (lo != lo) r = (r & 0xffff0000u) | encode_bf16(lo);
+    if (hi != hi) r = (r & 0x0000ffffu) | ((uint32_t)encode_bf16(hi) << 16);
+    return r;
 }
 
 // 2^x on the special-function unit (PTX ex2.approx.ftz: relative error about
