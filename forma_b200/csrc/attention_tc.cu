@@ -621,14 +621,18 @@ __global__ void attn_merge_kernel(AttnParams p) {
 }
 
 
-// Short key ranges (Lk <= 256; the ViT encoder's 197 tokens) at depth 64: one
-// CTA per (batch, head, 128-query tile), 192 threads, 256 TMEM columns and
-// ~81 KB of shared memory, so two CTAs share an SM.
-//   warp 0      TMA: the Q tile and every key and value row of the head (one
-//               or two 128-row boxes each; rows past Lk read as zeros).
+// Short key ranges (Lk <= 256; the ViT encoder's 197 tokens) at depth 64.  A
+// unit is one (batch, head, 128-query tile); CTAs are persistent (192
+// threads, 256 TMEM columns, ~81 KB of shared memory, two per SM) and take
+// units blockIdx.x, blockIdx.x + gridDim.x, ...
+//   warp 0      TMA: per unit the Q tile with every key row of the head (one
+//               or two 128-row boxes; rows past Lk read as zeros) as soon as
+//               the previous unit's S has read Q and K, and the value rows as
+//               soon as the previous unit's output has left the V buffer.
 //   warp 1      one S = Q K^T group over all keys (N = Lk rounded up to 16,
-//               at most 256) into TMEM columns [0, N); after the softmax, one
-//               O = P V group (K = N) into columns [128, 128 + D).
+//               at most 256) into TMEM columns [0, N), issued once the
+//               softmax has read the previous unit's O out of TMEM; after the
+//               softmax, one O = P V group (K = N) into columns [128, 128 + D).
 //   warps 2-5   the softmax of one query row per thread in two passes over the
 //               row in TMEM: the exact row maximum, then exp2 of every score,
 //               P packed to 16-bit pairs over the scores already read (P of
@@ -636,7 +640,9 @@ __global__ void attn_merge_kernel(AttnParams p) {
 //               has read), and the sum of the rounded weights.  With the whole
 //               row present there is no running maximum, no rescale and no
 //               second S round trip; O overwrites S columns the softmax has
-//               consumed.  Then O / l is stored.
+//               consumed.  Then O is read out of TMEM (which lets the next
+//               unit's S start), O / l is staged in the V buffer (free once PV
+//               is done) and written by TMA tensor stores.
 // BF16 weights carry the same 2^-shift pre-scale as attn_fwd_kernel, so the
 // numerator cannot overflow f32; fully masked rows (causal) produce zeros.
 constexpr int SD = 64;                          // depth
@@ -657,33 +663,23 @@ __global__ void __launch_bounds__(S_THREADS, 2) attn_short_kernel(const __grid_c
     unsigned char* sK = sQ + S_Q_BYTES;
     unsigned char* sV = sK + S_KV_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S_KV_BYTES);
-    uint64_t* qk_full = bars;
-    uint64_t* v_full = bars + 1;
-    uint64_t* s_full = bars + 2;
-    uint64_t* p_full = bars + 3;
-    uint64_t* o_full = bars + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+    uint64_t* qk_full = bars;       // Q and K of the unit landed
+    uint64_t* qk_empty = bars + 1;  // S of the unit computed: Q and K may reload
+    uint64_t* v_full = bars + 2;
+    uint64_t* v_empty = bars + 3;   // the unit's output has left the V buffer
+    uint64_t* s_full = bars + 4;
+    uint64_t* p_full = bars + 5;    // 128 arrivals
+    uint64_t* o_full = bars + 6;
+    uint64_t* o_free = bars + 7;    // 128 arrivals: O read out of TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t bh = blockIdx.x / p.q_blocks;
-    const uint32_t qb = blockIdx.x % p.q_blocks;
-    const uint32_t q0 = qb * TQ;
-    const uint32_t batch = bh / p.H, head = bh % p.H;
-    const int32_t kv_head = (int32_t)(head / (p.H / p.Hkv));
-    const int32_t k_b = p.k_batch_bcast ? 0 : (int32_t)batch, v_b = p.v_batch_bcast ? 0 : (int32_t)batch;
+    const uint32_t units = p.q_blocks * p.bh;
     const uint32_t nkb = p.kv_tiles;                      // 128-row key boxes (1 or 2)
     const uint32_t nkp = (p.Lk + 15u) & ~15u;             // keys rounded up to the MMA's N step
-    // keys visible to this tile's last query row (causal): none -> no MMA at all
-    int64_t last_vis = (int64_t)p.Lk - 1;
-    if (p.causal) {
-        int64_t last_q = (int64_t)min(q0 + TQ, p.L) - 1;
-        if (p.q_mod < p.L) last_q = min(last_q, (int64_t)p.q_mod - 1);
-        last_vis = min(last_vis, last_q + (int64_t)p.causal_offset);
-    }
-    const bool any = last_vis >= 0;
 
     if (threadIdx.x == 0) {
-        for (int b = 0; b < 5; ++b) mbar_init(&bars[b], b == 3 ? 128 : 1);
+        for (int b = 0; b < 8; ++b) mbar_init(&bars[b], b == 5 || b == 7 ? 128 : 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -696,175 +692,217 @@ __global__ void __launch_bounds__(S_THREADS, 2) attn_short_kernel(const __grid_c
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0 && any) {
-            mbar_arrive_expect_tx(qk_full, (uint32_t)(S_Q_BYTES + nkb * TK * SD * 2));
-            tma_load_4d(sQ, &tmQ, 0, (int32_t)q0, (int32_t)head, (int32_t)batch, qk_full);
-            for (uint32_t b = 0; b < nkb; ++b)
-                tma_load_4d(sK + b * (TK * 128), &tmK, 0, (int32_t)(b * TK), kv_head, k_b, qk_full);
-            mbar_arrive_expect_tx(v_full, (uint32_t)(nkb * TK * SD * 2));
-            for (uint32_t b = 0; b < nkb; ++b)
-                tma_load_4d(sV + b * (TK * 128), &tmV, 0, (int32_t)(b * TK), kv_head, v_b, v_full);
-            // the copies complete before the CTA's final barrier (bounded)
-            (void)mbar_wait(qk_full, 0);
-            (void)mbar_wait(v_full, 0);
+        if (lane == 0) {
+            bool failed = false;
+            uint32_t k = 0;
+            for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, ++k) {
+                const uint32_t bh = u / p.q_blocks, qb = u % p.q_blocks;
+                const uint32_t batch = bh / p.H, head = bh % p.H;
+                const int32_t kv_head = (int32_t)(head / (p.H / p.Hkv));
+                const int32_t k_b = p.k_batch_bcast ? 0 : (int32_t)batch, v_b = p.v_batch_bcast ? 0 : (int32_t)batch;
+                if (!mbar_wait(qk_empty, (k & 1) ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(qk_full, (uint32_t)(S_Q_BYTES + nkb * TK * SD * 2));
+                tma_load_4d(sQ, &tmQ, 0, (int32_t)(qb * TQ), (int32_t)head, (int32_t)batch, qk_full);
+                for (uint32_t b = 0; b < nkb; ++b)
+                    tma_load_4d(sK + b * (TK * 128), &tmK, 0, (int32_t)(b * TK), kv_head, k_b, qk_full);
+                if (!mbar_wait(v_empty, (k & 1) ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(v_full, (uint32_t)(nkb * TK * SD * 2));
+                for (uint32_t b = 0; b < nkb; ++b)
+                    tma_load_4d(sV + b * (TK * 128), &tmV, 0, (int32_t)(b * TK), kv_head, v_b, v_full);
+            }
+            // every copy this thread issued is consumed before the CTA's
+            // final barrier; after a failed wait, drain them (bounded)
+            if (failed) {
+                atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+                if (k > 0) (void)mbar_wait(v_full, (k - 1) & 1);
+                (void)mbar_wait(qk_full, k & 1);
+            }
         }
     } else if (warp == 1) {
         auto wait = [](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); };
-        bool ok = !any || wait(qk_full, 0);
-        if (ok && any) {
+        const uint32_t idesc_s = f16_idesc(p.fmt, TQ, nkp);
+        const uint32_t idesc_o = f16_idesc(p.fmt, TQ, SD) | (1u << 16);  // B (V) is MN-major
+        const uint64_t qd = sw128_desc(smem_u32(sQ)), kd = sw128_desc(smem_u32(sK));
+        const uint64_t vd = sw128_mn_desc(smem_u32(sV), TK * 128);
+        bool ok = true;
+        uint32_t k = 0;
+        for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++k) {
+            // S overwrites the previous unit's O columns: wait until they are read
+            ok = wait(qk_full, k & 1) && wait(o_free, (k & 1) ^ 1);
+            if (!ok) break;
             tc_fence_after();
-            const uint32_t idesc_s = f16_idesc(p.fmt, TQ, nkp);
-            const uint64_t qd = sw128_desc(smem_u32(sQ)), kd = sw128_desc(smem_u32(sK));
 #pragma unroll
-            for (int k = 0; k < SD / 16; ++k)
-                umma_f16_ss_warp(tmem, desc_add(qd, (uint32_t)(k * 32)), desc_add(kd, (uint32_t)(k * 32)), idesc_s, k != 0);
+            for (int kk = 0; kk < SD / 16; ++kk)
+                umma_f16_ss_warp(tmem, desc_add(qd, (uint32_t)(kk * 32)), desc_add(kd, (uint32_t)(kk * 32)), idesc_s, kk != 0);
             umma_commit_warp(s_full);
-            ok = wait(v_full, 0) && wait(p_full, 0);
-            if (ok) {
-                tc_fence_after();
-                const uint32_t idesc_o = f16_idesc(p.fmt, TQ, SD) | (1u << 16);  // B (V) is MN-major
-                const uint64_t vd = sw128_mn_desc(smem_u32(sV), TK * 128);
-                for (uint32_t k = 0; k < nkp / 16; ++k)
-                    umma_f16_ts_warp(tmem + S_O_COL, tmem + k * 8, desc_add(vd, k * 16 * 128), idesc_o, k != 0);
-                umma_commit_warp(o_full);
-            }
+            umma_commit_warp(qk_empty);
+            ok = wait(v_full, k & 1) && wait(p_full, k & 1);
+            if (!ok) break;
+            tc_fence_after();
+            for (uint32_t kk = 0; kk < nkp / 16; ++kk)
+                umma_f16_ts_warp(tmem + S_O_COL, tmem + kk * 8, desc_add(vd, kk * 16 * 128), idesc_o, kk != 0);
+            umma_commit_warp(o_full);
         }
         if (!ok && lane == 0) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
     } else {
         const int quarter = warp & 3;
         const uint32_t row = (uint32_t)(quarter * 32 + lane);
-        const uint32_t q = q0 + row;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const int64_t vis = p.causal ? (int64_t)(q % p.q_mod) + (int64_t)p.causal_offset : (int64_t)1 << 40;
-        const int64_t lim64 = min((int64_t)p.Lk, vis + 1);
-        const int32_t lim = (int32_t)(lim64 < 0 ? 0 : lim64);   // keys [0, lim) of this row are visible
         const float NEG = -__int_as_float(0x7f800000);
         const float sl = p.scale_log2;
         const uint32_t nch = (nkp + 31u) / 32u;                 // 32-column chunks holding keys
         const bool neg = sl < 0.0f;                               // logit maximum = min(x) * sl
-        bool ok = any;
-        float l = 0.0f;
-        if (ok && !__all_sync(0xffffffffu, mbar_wait(s_full, 0))) ok = false;
-        if (ok) {
-            tc_fence_after();
-            // pass 1: the extreme of the visible scores, four chunks per TMEM
-            // round trip; only chunks that reach past the row's last visible
-            // key are masked element by element
-            float ext = neg ? -NEG : NEG;
-            for (uint32_t c0 = 0; c0 < nch; c0 += 4) {
-                uint32_t r[4][32];
+        const bool storer = warp == 2 && lane == 0;
+        bool ok = true;
+        uint32_t k = 0;
+        for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++k) {
+            const uint32_t bh = u / p.q_blocks, qb = u % p.q_blocks;
+            const uint32_t q0 = qb * TQ, q = q0 + row;
+            const int64_t vis = p.causal ? (int64_t)(q % p.q_mod) + (int64_t)p.causal_offset : (int64_t)1 << 40;
+            const int64_t lim64 = min((int64_t)p.Lk, vis + 1);
+            const int32_t lim = (int32_t)(lim64 < 0 ? 0 : lim64);   // keys [0, lim) of this row are visible
+            float l = 0.0f;
+            // A failed wait is warp-uniform but not CTA-uniform: the warp still
+            // takes the epilogue (zeros) so that all four softmax warps meet at
+            // its named barrier, and leaves the loop after it.
+            bool good = __all_sync(0xffffffffu, mbar_wait(s_full, k & 1));
+            if (good) {
+                tc_fence_after();
+                // pass 1: the extreme of the visible scores, four chunks per TMEM
+                // round trip; only chunks that reach past the row's last visible
+                // key are masked element by element
+                float ext = neg ? -NEG : NEG;
+                for (uint32_t c0 = 0; c0 < nch; c0 += 4) {
+                    // chunks past nch are loaded too (every chunk lies inside the
+                    // 256 allocated columns) and ignored: loads under a condition
+                    // make the compiler keep two copies of the chunk registers
+                    uint32_t r[4][32];
 #pragma unroll
-                for (int b = 0; b < 4; ++b)
-                    if (c0 + b < nch) tmem_ld32(tmem + lane_base + (c0 + b) * 32, r[b]);
-                tmem_wait_ld();
+                    for (int b = 0; b < 4; ++b)
+                        tmem_ld32(tmem + lane_base + (c0 + b) * 32, r[b]);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    if (c0 + b >= nch) break;
-                    const int key0 = (int)((c0 + b) * 32);
-                    if (key0 + 32 <= lim) {
-                        float e0 = ext, e1 = ext;
+                    for (int b = 0; b < 4; ++b) {
+                        if (c0 + b >= nch) break;
+                        const int key0 = (int)((c0 + b) * 32);
+                        if (key0 + 32 <= lim) {
+                            float e0 = ext, e1 = ext;
 #pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            const float a0 = __uint_as_float(r[b][i]), a1 = __uint_as_float(r[b][i + 1]);
-                            const float a2 = __uint_as_float(r[b][i + 2]), a3 = __uint_as_float(r[b][i + 3]);
-                            e0 = neg ? min3n(e0, a0, a1) : max3n(e0, a0, a1);
-                            e1 = neg ? min3n(e1, a2, a3) : max3n(e1, a2, a3);
+                            for (int i = 0; i < 32; i += 4) {
+                                const float a0 = __uint_as_float(r[b][i]), a1 = __uint_as_float(r[b][i + 1]);
+                                const float a2 = __uint_as_float(r[b][i + 2]), a3 = __uint_as_float(r[b][i + 3]);
+                                e0 = neg ? min3n(e0, a0, a1) : max3n(e0, a0, a1);
+                                e1 = neg ? min3n(e1, a2, a3) : max3n(e1, a2, a3);
+                            }
+                            ext = neg ? fminf(e0, e1) : fmaxf(e0, e1);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (key0 + i < lim) ext = neg ? fminf(ext, __uint_as_float(r[b][i])) : fmaxf(ext, __uint_as_float(r[b][i]));
                         }
-                        ext = neg ? fminf(e0, e1) : fmaxf(e0, e1);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (key0 + i < lim) ext = neg ? fminf(ext, __uint_as_float(r[b][i])) : fmaxf(ext, __uint_as_float(r[b][i]));
                     }
                 }
-            }
-            const float mt = lim == 0 ? NEG : ext * sl;
-            const float base = mt == NEG ? 0.0f : mt + p.shift;
-            const float2 sl2 = make_float2(sl, sl), nb2 = make_float2(-base, -base);
-            // pass 2: P = exp2(x * sl - base) over the visible keys, 0 elsewhere,
-            // two chunks per TMEM round trip
-            float2 lsa[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            for (uint32_t c0 = 0; c0 < nch; c0 += 2) {
-                uint32_t r[2][32];
+                const float mt = lim == 0 ? NEG : ext * sl;
+                const float base = mt == NEG ? 0.0f : mt + p.shift;
+                const float2 sl2 = make_float2(sl, sl), nb2 = make_float2(-base, -base);
+                // pass 2: P = exp2(x * sl - base) over the visible keys, 0 elsewhere,
+                // two chunks per TMEM round trip
+                float2 lsa[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                for (uint32_t c0 = 0; c0 < nch; c0 += 2) {
+                    uint32_t r[2][32];
 #pragma unroll
-                for (int b = 0; b < 2; ++b)
-                    if (c0 + b < nch) tmem_ld32(tmem + lane_base + (c0 + b) * 32, r[b]);
-                tmem_wait_ld();
+                    for (int b = 0; b < 2; ++b)
+                        tmem_ld32(tmem + lane_base + (c0 + b) * 32, r[b]);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    if (c0 + b >= nch) break;
-                    const int key0 = (int)((c0 + b) * 32);
-                    const bool full = key0 + 32 <= lim;
-                    uint32_t pk[16];
+                    for (int b = 0; b < 2; ++b) {
+                        if (c0 + b >= nch) break;
+                        const int key0 = (int)((c0 + b) * 32);
+                        const bool full = key0 + 32 <= lim;
+                        uint32_t pk[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float2 z = __ffma2_rn(make_float2(__uint_as_float(r[b][2 * i]), __uint_as_float(r[b][2 * i + 1])), sl2, nb2);
-                        if (!full) {
-                            z.x = key0 + 2 * i < lim ? z.x : NEG;
-                            z.y = key0 + 2 * i + 1 < lim ? z.y : NEG;
+                        for (int i = 0; i < 16; ++i) {
+                            float2 z = __ffma2_rn(make_float2(__uint_as_float(r[b][2 * i]), __uint_as_float(r[b][2 * i + 1])), sl2, nb2);
+                            if (!full) {
+                                z.x = key0 + 2 * i < lim ? z.x : NEG;
+                                z.y = key0 + 2 * i + 1 < lim ? z.y : NEG;
+                            }
+                            const float2 e = (i & 7) == 7 ? ex2_poly2(z) : make_float2(ex2(z.x), ex2(z.y));
+                            pk[i] = pack2(e.x, e.y, p.fmt);
+                            lsa[i & 1] = __fadd2_rn(lsa[i & 1], e);
                         }
-                        const float2 e = (i & 7) == 7 ? ex2_poly2(z) : make_float2(ex2(z.x), ex2(z.y));
-                        pk[i] = pack2(e.x, e.y, p.fmt);
-                        lsa[i & 1] = __fadd2_rn(lsa[i & 1], e);
+                        tmem_st16(tmem + lane_base + (c0 + b) * 16, pk);
                     }
-                    tmem_st16(tmem + lane_base + (c0 + b) * 16, pk);
                 }
+                tmem_wait_st();
+                const float2 l2 = __fadd2_rn(lsa[0], lsa[1]);
+                l = l2.x + l2.y;
+                tc_fence_before();
+                mbar_arrive(p_full);
+                good = __all_sync(0xffffffffu, mbar_wait(o_full, k & 1));
             }
-            tmem_wait_st();
-            const float2 l2 = __fadd2_rn(lsa[0], lsa[1]);
-            l = l2.x + l2.y;
-            tc_fence_before();
-            mbar_arrive(p_full);
-            if (!__all_sync(0xffffffffu, mbar_wait(o_full, 0))) ok = false;
-        }
-        if (any && !ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
-        tc_fence_after();
-        // Epilogue: O / l staged in shared memory (the key buffer, free once
-        // S is computed) in the 128-byte-swizzled layout of the output's
-        // tensor map, then written by one TMA tensor store per 128-byte-wide
-        // box (rows past L are clipped by the map).
-        const bool load = ok;  // warp-uniform
-        uint32_t o[SD];
-        if (load) {
+            uint32_t o[SD];
+            if (good) {
+                tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < SD / 32; ++c) tmem_ld32(tmem + lane_base + S_O_COL + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
-            tmem_wait_ld();
-        } else {
+                for (int c = 0; c < SD / 32; ++c)
+                    tmem_ld32(tmem + lane_base + S_O_COL + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(o_free);  // the next unit's S may overwrite O's columns
+            } else {
 #pragma unroll
-            for (int i = 0; i < SD; ++i) o[i] = 0u;
-        }
-        const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
-        const uint32_t swz = row & 7;
-        if (p.out_low) {
-            unsigned char* dst = sK + row * 128;  // one box: 64 16-bit values per row
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<uint4*>(dst + ((j ^ swz) * 16)) = make_uint4(
-                    encode_low_pair(__uint_as_float(o[8 * j]) * inv, __uint_as_float(o[8 * j + 1]) * inv, p.out_low),
-                    encode_low_pair(__uint_as_float(o[8 * j + 2]) * inv, __uint_as_float(o[8 * j + 3]) * inv, p.out_low),
-                    encode_low_pair(__uint_as_float(o[8 * j + 4]) * inv, __uint_as_float(o[8 * j + 5]) * inv, p.out_low),
-                    encode_low_pair(__uint_as_float(o[8 * j + 6]) * inv, __uint_as_float(o[8 * j + 7]) * inv, p.out_low));
-        } else {
-#pragma unroll
-            for (int b = 0; b < SD / 32; ++b) {  // boxes of 32 f32 per row
-                unsigned char* dst = sK + b * (TQ * 128) + row * 128;
+                for (int i = 0; i < SD; ++i) o[i] = 0u;
+                l = 0.0f;
+            }
+            // Epilogue: O / l staged in the V buffer (PV has read it) in the
+            // 128-byte-swizzled layout of the output's tensor map, then written
+            // by one TMA tensor store per 128-byte-wide box (rows past L are
+            // clipped by the map); the V buffer is handed back to the producer
+            // once the stores have read it.
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const uint32_t swz = row & 7;
+            if (p.out_low) {
+                unsigned char* dst = sV + row * 128;  // one box: 64 16-bit values per row
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float4*>(dst + ((j ^ swz) * 16)) =
-                        make_float4(__uint_as_float(o[32 * b + 4 * j]) * inv, __uint_as_float(o[32 * b + 4 * j + 1]) * inv,
-                                    __uint_as_float(o[32 * b + 4 * j + 2]) * inv, __uint_as_float(o[32 * b + 4 * j + 3]) * inv);
+                    *reinterpret_cast<uint4*>(dst + ((j ^ swz) * 16)) = make_uint4(
+                        encode_low_pair(__uint_as_float(o[8 * j]) * inv, __uint_as_float(o[8 * j + 1]) * inv, p.out_low),
+                        encode_low_pair(__uint_as_float(o[8 * j + 2]) * inv, __uint_as_float(o[8 * j + 3]) * inv, p.out_low),
+                        encode_low_pair(__uint_as_float(o[8 * j + 4]) * inv, __uint_as_float(o[8 * j + 5]) * inv, p.out_low),
+                        encode_low_pair(__uint_as_float(o[8 * j + 6]) * inv, __uint_as_float(o[8 * j + 7]) * inv, p.out_low));
+            } else {
+#pragma unroll
+                for (int b = 0; b < SD / 32; ++b) {  // boxes of 32 f32 per row
+                    unsigned char* dst = sV + b * (TQ * 128) + row * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(dst + ((j ^ swz) * 16)) =
+                            make_float4(__uint_as_float(o[32 * b + 4 * j]) * inv, __uint_as_float(o[32 * b + 4 * j + 1]) * inv,
+                                        __uint_as_float(o[32 * b + 4 * j + 2]) * inv, __uint_as_float(o[32 * b + 4 * j + 3]) * inv);
+                }
             }
+            fence_proxy_async_smem();
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps' rows are staged
+            if (storer) {
+                const uint32_t batch = bh / p.H, head = bh % p.H;
+                const int boxes = p.out_low ? 1 : SD / 32;
+                for (int b = 0; b < boxes; ++b)
+                    tma_store_4d(&tmO, b * (p.out_low ? 64 : 32), (int32_t)q0, (int32_t)head, (int32_t)batch,
+                                 sV + b * (TQ * 128));
+                bulk_commit_group();
+                bulk_wait_read_all();  // the V buffer stays valid until the stores have read it
+                mbar_arrive(v_empty);
+            }
+            if (!good) ok = false;
         }
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps' rows are staged
-        if (warp == 2 && lane == 0) {
-            const int boxes = p.out_low ? 1 : SD / 32;
-            for (int b = 0; b < boxes; ++b)
-                tma_store_4d(&tmO, b * (p.out_low ? 64 : 32), (int32_t)q0, (int32_t)head, (int32_t)batch,
-                             sK + b * (TQ * 128));
-            bulk_commit_group();
-            bulk_wait_read_all();  // shared memory stays valid until the stores have read it
-        }
+        if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
         tc_fence_before();
     }
     __syncthreads();
@@ -1117,9 +1155,10 @@ int launch_short(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const Ro
     if (!make_out_map(&to, p.out, p.out_low, SD, ol)) return FB_ERR_UNSUPPORTED;
     if (cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM) != cudaSuccess)
         return launch_status("shared-memory attribute");
-    const uint64_t grid = (uint64_t)p.q_blocks * BH;
-    if (grid == 0) return FB_OK;
-    if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
+    const uint64_t units = (uint64_t)p.q_blocks * BH;
+    if (units == 0) return FB_OK;
+    if (units > 0xffffffffull) return FB_ERR_UNSUPPORTED;
+    const uint64_t grid = std::min<uint64_t>(units, (uint64_t)sm_count() * 2);  // persistent, two CTAs per SM
     attn_short_kernel<<<(unsigned)grid, S_THREADS, S_SMEM, st>>>(tq, tk, tv, to, p);
     count_launch("attn_short_kernel");
     return launch_status("kernel launch");
