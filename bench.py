@@ -733,6 +733,13 @@ def run_profile(args) -> int:
             fn = lambda: api.conv_low_into(xin, w, one, ov)  # noqa: E731
         else:
             fn = lambda: api.conv_low_gelu_into(xin, w, one, ov)  # noqa: E731
+    elif name == "c5_attn":
+        # one C5 layer's attention: [64, 12 heads, 197 tokens, 64] BF16 views of
+        # the packed QKV rows, BF16 rows out
+        qkv = torch.randn(64, 197, 3, 12, 64, device=dev, generator=g).bfloat16()
+        qv, kv, vv = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+        out = torch.empty(64, 197, 12, 64, dtype=torch.bfloat16, device=dev)
+        fn = lambda: api.attention_low_into(qv, kv, vv, None, AttentionOptions(), out.permute(0, 2, 1, 3))  # noqa: E731
     elif name == "vit_c5":
         from forma_b200.vit import ViTConfig, ViTEncoder
 
