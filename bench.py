@@ -733,6 +733,15 @@ def run_profile(args) -> int:
             fn = lambda: api.conv_low_into(xin, w, one, ov)  # noqa: E731
         else:
             fn = lambda: api.conv_low_gelu_into(xin, w, one, ov)  # noqa: E731
+    elif name == "c5_proj":
+        # the C5 attention output projection: [64*197, 768] x [768, 768] added
+        # into the f32 tokens in the GEMM epilogue
+        t = torch.randn(64, 197, 768, device=dev, generator=g).bfloat16()
+        w = (torch.randn(768, 768, 1, 1, device=dev, generator=g) * 768 ** -0.5).bfloat16()
+        x = torch.randn(64, 1, 197, 768, device=dev, generator=g)
+        xin, xv = t.view(64, 1, 197, 768).permute(0, 3, 1, 2), x.permute(0, 3, 1, 2)
+        one = ConvOptions([1, 1], [1, 1], [0, 0], [0, 0])
+        fn = lambda: api.conv_low_f32_accumulate(xin, w, one, xv)  # noqa: E731
     elif name == "c5_attn":
         # one C5 layer's attention: [64, 12 heads, 197 tokens, 64] BF16 views of
         # the packed QKV rows, BF16 rows out
