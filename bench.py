@@ -389,7 +389,8 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     record("attention_bf16_decode_gqa",
            (lambda: api.attention_low_f32(q[:n], k[:n], v[:n], None, AttentionOptions())) if n else (lambda: None),
            4 * 8 * 32 * 1 * 8192 * 128, pk["bf16_tflops"], "measured bf16 dense (burst)",
-           "GQA heads packed into one tile per key/value head, key range split across CTAs",
+           "the 4 query heads of a key/value head as one 16-row block on the warp-level MMA, K/V streamed once "
+           "through per-warp cp.async rings, key ranges merged on the device",
            nbytes=2 * 8 * 8 * 8192 * 128 * 2 + 8 * 32 * 128 * 2 + 8 * 32 * 128 * 4, shard=f"batches {b0}:{b1} of 8")
     del q, k, v
     # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32

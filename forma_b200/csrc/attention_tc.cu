@@ -589,13 +589,18 @@ __global__ void attn_merge_kernel(AttnParams p) {
     for (uint64_t w = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
         const uint64_t bh = w / p.L, q = w % p.L;
         const float* rec = p.part + ((bh * p.rec_rows + q) * p.splits) * (D + 2);
+        // the largest base of the ranges that saw a key, lanes over ranges
         float M = -__int_as_float(0x7f800000);
-        for (uint32_t s = 0; s < p.splits; ++s)
+        for (uint32_t s = lane; s < p.splits; s += 32)
             if (rec[s * (D + 2) + 1] > 0.0f) M = fmaxf(M, rec[s * (D + 2)]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.0f;
         float o[D / 32];
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) o[i] = 0.0f;
+        // ranges in index order (four records' loads in flight at once)
+#pragma unroll 4
         for (uint32_t s = 0; s < p.splits; ++s) {
             const float* r = rec + s * (D + 2);
             const float l = r[1];
@@ -1085,6 +1090,374 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
 }
 
 
+// ---------------------------------------------------------------- decode
+// Decode-shaped 16-bit attention: the G x L query rows that share one key/
+// value head (G query heads of a GQA group, L <= 16 / G queries each) form a
+// single 16-row block, and every key is read once from HBM for all of them.
+// A 128-row tcgen05 tile would carry at most 16 valid rows and its per-key
+// softmax cost is that of 128 rows, so this path runs the block on the warp-
+// level tensor-core MMA (m16n8k16, f32 accumulation) with the operands loaded
+// straight from global memory into registers: the kernel is bound by the
+// K/V read (HBM), not by arithmetic.
+//   A CTA owns one key range of one (batch, key/value head); each of its four
+//   warps walks a quarter of it 16 keys at a time, the keys streamed through
+//   its own three-stage cp.async ring in shared memory (two stages in flight
+//   while one is consumed): S = Q K^T (two n8 tiles, D/16 k-steps), online
+//   softmax on the accumulator fragments (row maxima over the four lanes of a
+//   row), P packed to 16-bit pairs in registers as the A operand of O += P V
+//   (D/8 n8 tiles).  The four warps combine their partial results through
+//   shared memory and the CTA leaves {base, l, O[D]} per query row for
+//   attn_merge_kernel, as the key-split tensor-core path does.
+//   Depth permutation: the contraction over the depth is order-free, so lane
+//   (g, c) (g = lane / 4, c = lane % 4) takes as its k-step s operand words the
+//   depth pairs (c*D/4 + 4s, +1) and (c*D/4 + 4s + 2, +3) of Q and K: every
+//   lane's Q and K fragments are one contiguous D/4-value run per row (16-byte
+//   loads).  Likewise the output columns of PV tile j are permuted so that
+//   lane group g supplies V columns g*D/8 .. g*D/8 + D/8 - 1 (contiguous) and
+//   lane (g, c) receives O columns [2c*D/8, (2c+2)*D/8) of its rows.
+//   BF16 weights carry the 2^-shift pre-scale of attn_fwd_kernel (no f32
+//   overflow for V near the format's maximum); the row sum adds the rounded
+//   weights the MMA multiplies.
+struct Dec16Params {
+    const uint16_t* q;
+    const uint16_t* k;
+    const uint16_t* v;
+    uint64_t q_sb, q_sh, q_sl;  // element strides: batch, head, query row (depth contiguous)
+    uint64_t k_sb, k_sh, k_sk;  // batch (0: shared), key/value head, key
+    uint64_t v_sb, v_sh, v_sk;
+    uint32_t H, Hkv, G, L, Lk;
+    uint32_t splits, keys_per_split;  // CTAs (key ranges) per (batch, key/value head); keys per warp
+    float scale_log2, shift;
+    int32_t causal, causal_offset;
+    float* part;  // records [((batch * H + head) * L + query) * splits + range] x {base, l, O[D]}
+};
+
+template <int FMT>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    if constexpr (FMT == 1)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int FMT>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+    if constexpr (FMT == 1) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    else return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+constexpr int DEC_WARPS = 4;
+constexpr int DEC_STAGES = 3;  // 16-key stages per warp: two in flight while one is consumed
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared-memory positions (16-byte chunks) of a stage's K and V rows: XOR
+// swizzles under which every 8-lane phase of the fragment reads below touches
+// eight distinct 16-byte bank groups.  K: lane (g, c) reads chunks
+// c*D/32 .. of rows g and 8 + g; V: chunk(s) g*D/64 .. of rows 2c, 2c+1,
+// 2c+8, 2c+9.
+template <int D>
+__device__ __forceinline__ uint32_t k_chunk(uint32_t row, uint32_t chunk) {
+    if constexpr (D == 128) return chunk ^ (((chunk >> 3) & 1u) | ((row & 1u) << 1));
+    else return chunk ^ (row & 1u);
+}
+__device__ __forceinline__ uint32_t v_chunk(uint32_t row, uint32_t chunk) { return chunk ^ (((row >> 1) & 3u) << 1); }
+
+template <int D, int FMT>
+__global__ void __launch_bounds__(32 * DEC_WARPS) attn_decode16_kernel(Dec16Params p) {
+    constexpr int QW = D / 8;    // operand words (16-bit pairs) per lane per row: D / 4 values
+    constexpr int KS = D / 16;   // k-steps of S
+    constexpr int NJ = D / 8;    // n8 tiles of O
+    constexpr int CPR = D / 8;   // 16-byte chunks per K / V row
+    constexpr int STAGE = 2 * 16 * CPR;  // chunks per stage: 16 K rows then 16 V rows
+    extern __shared__ uint4 dsm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    uint4* ring = dsm + (size_t)warp * DEC_STAGES * STAGE;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+    const uint32_t unit = blockIdx.x / p.splits;  // (batch, key/value head)
+    const uint32_t split = blockIdx.x % p.splits;  // this CTA's key range; warp w takes its w-th quarter
+    const uint32_t b = unit / p.Hkv, hkv = unit % p.Hkv;
+    const uint32_t R = p.G * p.L;
+    const uint32_t k_begin = min((split * DEC_WARPS + warp) * p.keys_per_split, p.Lk);
+    const uint32_t k_end = min(k_begin + p.keys_per_split, p.Lk);  // may be empty: the warp only joins the combine
+    const float NEG = -__int_as_float(0x7f800000);
+
+    // Q fragments of rows g and g + 8 (zeros past R)
+    uint32_t qa[2][QW];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const uint32_t r = (uint32_t)(g + 8 * rr);
+        if (r < R) {
+            const uint32_t h = hkv * p.G + r / p.L, l = r % p.L;
+            const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.q_sb + h * p.q_sh + l * p.q_sl + c * (D / 4));
+#pragma unroll
+            for (int i = 0; i < QW / 4; ++i) {
+                const uint4 w = src[i];
+                qa[rr][4 * i] = w.x, qa[rr][4 * i + 1] = w.y, qa[rr][4 * i + 2] = w.z, qa[rr][4 * i + 3] = w.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < QW; ++i) qa[rr][i] = 0u;
+        }
+    }
+    // causal visibility of rows g, g + 8: key <= query + offset
+    int64_t vis[2];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const uint32_t r = (uint32_t)(g + 8 * rr);
+        vis[rr] = r >= R ? -1 : p.causal ? (int64_t)(r % p.L) + p.causal_offset : (int64_t)1 << 40;
+    }
+    const uint16_t* kbase = p.k + (uint64_t)b * p.k_sb + (uint64_t)hkv * p.k_sh;
+    const uint16_t* vbase = p.v + (uint64_t)b * p.v_sb + (uint64_t)hkv * p.v_sh;
+    // One stage: keys k0 .. k0 + 15 of K then V, 16 bytes per copy; keys past
+    // the range are zero-filled (source size 0, the address stays in bounds).
+    auto issue = [&](uint32_t k0, int slot) {
+        const uint32_t dst0 = ring_s + (uint32_t)(slot * STAGE * 16);
+#pragma unroll
+        for (int n = 0; n < STAGE / 32; ++n) {
+            const uint32_t e = (uint32_t)(lane + 32 * n);
+            const uint32_t kv = e / (16 * CPR), row = (e / CPR) % 16, chunk = e % CPR;
+            const uint32_t key = k0 + row;
+            const bool in = key < k_end;
+            const uint16_t* src = kv ? vbase + (uint64_t)(in ? key : k_begin) * p.v_sk + chunk * 8
+                                     : kbase + (uint64_t)(in ? key : k_begin) * p.k_sk + chunk * 8;
+            const uint32_t pc = kv ? v_chunk(row, chunk) : k_chunk<D>(row, chunk);
+            cp_async16(dst0 + (kv * 16 * CPR + row * CPR + pc) * 16, src, in ? 16u : 0u);
+        }
+    };
+    float o[NJ][4];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float m[2] = {NEG, NEG}, l[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int st = 0; st < DEC_STAGES - 1; ++st) {
+        if (k_begin + 16 * st < k_end) issue(k_begin + 16 * st, st);
+        cp_async_commit();
+    }
+    int slot = 0;
+    for (uint32_t k0 = k_begin; k0 < k_end; k0 += 16) {
+        cp_async_wait<DEC_STAGES - 2>();  // this stage's copies (all but the newest group) have landed
+        __syncwarp();
+        const uint4* kst = ring + slot * STAGE;
+        const uint4* vst = kst + 16 * CPR;
+        float s[2][4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            uint32_t kw[QW];
+            const uint32_t row = (uint32_t)(8 * t + g);
+#pragma unroll
+            for (int i = 0; i < QW / 4; ++i) {
+                const uint4 w = kst[row * CPR + k_chunk<D>(row, (uint32_t)(c * (QW / 4) + i))];
+                kw[4 * i] = w.x, kw[4 * i + 1] = w.y, kw[4 * i + 2] = w.z, kw[4 * i + 3] = w.w;
+            }
+            s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+                mma16816<FMT>(s[t], qa[0][2 * ks], qa[1][2 * ks], qa[0][2 * ks + 1], qa[1][2 * ks + 1], kw[2 * ks],
+                              kw[2 * ks + 1]);
+        }
+        // V words of keys 2c, 2c+1, 2c+8, 2c+9 at columns g*D/8 .. (D = 128:
+        // two chunks, read in the order that keeps each 8-lane phase on
+        // distinct bank groups)
+        uint32_t vw[4][NJ / 2];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t row = (uint32_t)(2 * c + (t & 1) + 8 * (t >> 1));
+            if constexpr (NJ / 8 == 2) {
+                const uint32_t odd = (uint32_t)(g & 1);
+                const uint4 w0 = vst[row * CPR + v_chunk(row, (uint32_t)(2 * g) + odd)];
+                const uint4 w1 = vst[row * CPR + v_chunk(row, (uint32_t)(2 * g) + (odd ^ 1u))];
+                const uint4 lo = odd ? w1 : w0, hi = odd ? w0 : w1;
+                vw[t][0] = lo.x, vw[t][1] = lo.y, vw[t][2] = lo.z, vw[t][3] = lo.w;
+                vw[t][4] = hi.x, vw[t][5] = hi.y, vw[t][6] = hi.z, vw[t][7] = hi.w;
+            } else {
+                const uint4 w = vst[row * CPR + v_chunk(row, (uint32_t)g)];
+                vw[t][0] = w.x, vw[t][1] = w.y, vw[t][2] = w.z, vw[t][3] = w.w;
+            }
+        }
+        __syncwarp();  // every lane has read this slot: it may be refilled
+        if (k0 + 16 * (DEC_STAGES - 1) < k_end) issue(k0 + 16 * (DEC_STAGES - 1), (slot + DEC_STAGES - 1) % DEC_STAGES);
+        cp_async_commit();
+        slot = slot + 1 == DEC_STAGES ? 0 : slot + 1;
+        // scores in log2 units, masked: s[t][e] is row g + 8 * (e >> 1), key k0 + 8t + 2c + (e & 1)
+        float mx[2] = {NEG, NEG};
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int rr = e >> 1;
+                const int64_t key = (int64_t)k0 + 8 * t + 2 * c + (e & 1);
+                const float x = (key < (int64_t)k_end && key <= vis[rr]) ? s[t][e] * p.scale_log2 : NEG;
+                s[t][e] = x;
+                mx[rr] = fmaxf(mx[rr], x);
+            }
+        float alpha[2], base[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+            mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+            const float mn = fmaxf(m[rr], mx[rr]);
+            alpha[rr] = m[rr] == NEG ? 0.0f : ex2(m[rr] - mn);
+            m[rr] = mn;
+            base[rr] = mn == NEG ? 0.0f : mn + p.shift;
+        }
+        // P as the A operand of PV: rows g / g + 8, keys 2c, 2c+1 (tile 0) and 8 + 2c, 9 + 2c (tile 1)
+        uint32_t pa[4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+                pa[2 * t + rr] = pack2(ex2(s[t][2 * rr] - base[rr]), ex2(s[t][2 * rr + 1] - base[rr]), FMT);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const float2 w0 = unpack2<FMT>(pa[rr]), w1 = unpack2<FMT>(pa[2 + rr]);
+            l[rr] = fmaf(l[rr], alpha[rr], (w0.x + w0.y) + (w1.x + w1.y));
+        }
+        if (__any_sync(0xffffffffu, alpha[0] != 1.0f || alpha[1] != 1.0f)) {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                o[j][0] *= alpha[0], o[j][1] *= alpha[0];
+                o[j][2] *= alpha[1], o[j][3] *= alpha[1];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;  // high or low 16-bit halves of the word pair
+            const uint32_t b0 = __byte_perm(vw[0][j / 2], vw[1][j / 2], sel);
+            const uint32_t b1 = __byte_perm(vw[2][j / 2], vw[3][j / 2], sel);
+            mma16816<FMT>(o[j], pa[0], pa[1], pa[2], pa[3], b0, b1);
+        }
+    }
+    cp_async_wait<0>();
+    // The CTA's four warps combine their ranges: each leaves {m, l, O} per
+    // row in its own (drained) ring, then the CTA writes one record per row,
+    // O = sum_w O_w 2^(m_w - M), l = sum_w l_w 2^(m_w - M) with M the largest
+    // m of the warps that saw a key.
+    float* xs = reinterpret_cast<float*>(ring);  // [16 rows][D + 2]: m, l, O
+    __syncwarp();
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 1);
+        l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 2);
+        float* x = xs + (g + 8 * rr) * (D + 2);
+        if (c == 0) {
+            x[0] = m[rr];
+            x[1] = l[rr];
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            x[2 + 2 * c * NJ + j] = o[j][2 * rr];
+            x[2 + (2 * c + 1) * NJ + j] = o[j][2 * rr + 1];
+        }
+    }
+    __syncthreads();
+    for (uint32_t r = 0; r < R; ++r) {
+        float mw[DEC_WARPS], lw[DEC_WARPS], M = NEG;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) {
+            const float* x = reinterpret_cast<const float*>(dsm + (size_t)w * DEC_STAGES * STAGE) + r * (D + 2);
+            mw[w] = x[0], lw[w] = x[1];
+            if (lw[w] > 0.0f) M = fmaxf(M, mw[w]);
+        }
+        float wt[DEC_WARPS], Lr = 0.0f;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) {
+            wt[w] = lw[w] > 0.0f ? exp2f(mw[w] - M) : 0.0f;
+            Lr = fmaf(lw[w], wt[w], Lr);
+        }
+        const uint32_t h = hkv * p.G + r / p.L, q = r % p.L;
+        float* rec = p.part + ((((uint64_t)b * p.H + h) * p.L + q) * p.splits + split) * (D + 2);
+        if (threadIdx.x == 0) {
+            rec[0] = M == NEG ? 0.0f : M + p.shift;
+            rec[1] = Lr;
+        }
+        for (uint32_t d = threadIdx.x; d < (uint32_t)D; d += 32 * DEC_WARPS) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < DEC_WARPS; ++w)
+                if (wt[w] != 0.0f)
+                    acc = fmaf(reinterpret_cast<const float*>(dsm + (size_t)w * DEC_STAGES * STAGE)[r * (D + 2) + 2 + d], wt[w], acc);
+            rec[2 + d] = acc;
+        }
+    }
+}
+
+// Decode path for 16-bit Q/K/V: FB_ERR_UNSUPPORTED unless at most 16 query
+// rows share a key/value head, keys are many, and every row is 16-byte
+// aligned (the merge writes the output rows).
+template <int D>
+int launch_decode16(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLayout& kl, const RowsLayout& vl,
+                    const RowsLayout& ol, uint64_t L, uint64_t H, uint64_t Hkv, cudaStream_t st) {
+    const uint64_t Lk = a.keys, G = H / Hkv, R = G * L;
+    if (R > 16 || Lk < 1024 || a.mask_kind != FB_MASK_NONE) return FB_ERR_UNSUPPORTED;
+    auto rows16 = [](const RowsLayout& rl) { return rl.s_row % 8 == 0 && rl.s_head % 8 == 0 && rl.s_batch % 8 == 0; };
+    if (!rows16(ql) || !rows16(kl) || !rows16(vl)) return FB_ERR_UNSUPPORTED;
+    if (Lk > 0x7fffffffull || ql.batch * H * L > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
+    const uint64_t B = ql.batch, units = B * Hkv;
+    // Key ranges: about two CTAs (of four warps) per SM, at least 256 keys
+    // per warp; `splits` CTAs per (batch, key/value head), each leaving one
+    // record per query row.
+    const uint64_t target = (uint64_t)sm_count() * 2;
+    const uint64_t want = std::max<uint64_t>(1, std::min<uint64_t>(target / units, (Lk + 256 * DEC_WARPS - 1) / (256 * DEC_WARPS)));
+    const uint64_t kps = ((Lk + want * DEC_WARPS - 1) / (want * DEC_WARPS) + 15) / 16 * 16;  // keys per warp
+    const uint64_t splits = (Lk + kps * DEC_WARPS - 1) / (kps * DEC_WARPS);
+    const uint64_t bytes = B * H * L * splits * (D + 2) * sizeof(float);
+    float* part = static_cast<float*>(scratch(st, bytes, SCRATCH_ATTN_SPLIT));
+    if (!part) {  // none (e.g. first use inside a graph capture): the tile kernel takes it
+        (void)cudaGetLastError();
+        return FB_ERR_UNSUPPORTED;
+    }
+    Dec16Params d{};
+    d.q = static_cast<const uint16_t*>(a.q) + a.q_offset;
+    d.k = static_cast<const uint16_t*>(a.k) + a.k_offset;
+    d.v = static_cast<const uint16_t*>(a.v) + a.v_offset;
+    d.q_sb = ql.s_batch, d.q_sh = ql.s_head, d.q_sl = ql.s_row;
+    d.k_sb = kl.batch_bcast ? 0 : kl.s_batch, d.k_sh = kl.s_head, d.k_sk = kl.s_row;
+    d.v_sb = vl.batch_bcast ? 0 : vl.s_batch, d.v_sh = vl.s_head, d.v_sk = vl.s_row;
+    d.H = (uint32_t)H, d.Hkv = (uint32_t)Hkv, d.G = (uint32_t)G, d.L = (uint32_t)L, d.Lk = (uint32_t)Lk;
+    d.splits = (uint32_t)splits, d.keys_per_split = (uint32_t)kps;
+    d.scale_log2 = a.scale * 1.4426950408889634f;
+    d.shift = fmt ? 9.0f + std::ceil(std::log2((float)std::max<uint64_t>(Lk, 1))) : 0.0f;
+    d.causal = a.causal ? 1 : 0;
+    d.causal_offset = a.causal_offset;
+    d.part = part;
+    const uint64_t grid = units * splits;
+    if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
+    const int smem = DEC_WARPS * DEC_STAGES * 2 * 16 * D * 2;  // bytes of the per-warp rings
+    auto kernel = fmt ? attn_decode16_kernel<D, 1> : attn_decode16_kernel<D, 0>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return launch_status("shared-memory attribute");
+    kernel<<<(unsigned)grid, 32 * DEC_WARPS, smem, st>>>(d);
+    count_launch(kernel_name("attn_decode16_kernel", {D, (int)fmt}).c_str());
+    if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
+    AttnParams m{};
+    m.L = (uint32_t)L, m.H = (uint32_t)H, m.bh = (uint32_t)(B * H), m.rec_rows = (uint32_t)L;
+    m.splits = (uint32_t)splits, m.part = part;
+    m.out = a.out_low ? reinterpret_cast<float*>(reinterpret_cast<uint16_t*>(a.out) + a.o_offset) : a.out + a.o_offset;
+    m.out_low = a.out_low;
+    m.o_sb = ol.s_batch, m.o_sh = ol.s_head, m.o_sl = ol.s_row;
+    const uint64_t rows = B * H * L;
+    const unsigned mgrid = (unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sm_count() * 16);
+    attn_merge_kernel<D><<<mgrid, 256, 0, st>>>(m);
+    count_launch(kernel_name("attn_merge_kernel", {D}).c_str());
+    return launch_status("kernel launch");
+}
+
 // Output rows [batch, heads, rows, D] as a 4-D TMA store target: 16-bit
 // (out_low = FB_BF16 / FB_F16, boxes of 64 values) or f32 (boxes of 32), 128
 // rows per box, 128-byte swizzle.
@@ -1218,6 +1591,13 @@ int launch_attention_tc(const AttnArgs& a, void* stream) {
         return FB_ERR_UNSUPPORTED;
     const uint32_t fmt = a.dtype == FB_BF16 ? 1 : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Decode (at most 16 query rows per key/value head over many keys): one
+    // 16-row block per head on the warp-level MMA, K/V read once.
+    if (a.mask_kind == FB_MASK_NONE && a.group_size * L <= 16) {
+        const int r1 = D == 64 ? launch_decode16<64>(a, fmt, ql, kl, vl, ol, L, H, Hkv, st)
+                               : launch_decode16<128>(a, fmt, ql, kl, vl, ol, L, H, Hkv, st);
+        if (r1 != FB_ERR_UNSUPPORTED) return r1;
+    }
     // Decode of grouped heads (few query rows, no mask): the G query heads of
     // a key/value head share its K/V, so their G x L rows become the rows of
     // one packed head (G times fewer key steps), when each head's rows of Q
