@@ -700,6 +700,12 @@ def run_profile(args) -> int:
         k_ = torch.randn(b, 32, 4096, 128, device=dev, generator=g).bfloat16()
         v = torch.randn(b, 32, 4096, 128, device=dev, generator=g).bfloat16()
         fn = lambda: api.attention_low_f32(q, k_, v, None, AttentionOptions(causal=0))  # noqa: E731
+    elif name == "decode_gqa":
+        # the decode entry: one query per head, 32 query heads over 8 key/value heads, 8192 keys, D 128
+        q = torch.randn(8, 32, 1, 128, device=dev, generator=g).bfloat16()
+        k_ = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
+        v = torch.randn(8, 8, 8192, 128, device=dev, generator=g).bfloat16()
+        fn = lambda: api.attention_low_f32(q, k_, v, None, AttentionOptions())  # noqa: E731
     elif name == "conv_c1":
         x = torch.rand(8, 64, 56, 56, device=dev, generator=g) * 2 - 1
         w = torch.randn(64, 64, 3, 3, device=dev, generator=g) * 0.06
