@@ -432,7 +432,8 @@ def run_ops(api, dev, dist, args, pk) -> dict:
 def cpu_baseline_ops() -> dict:
     """The oracle (the reference's f64 algorithms) on the host's cores on one
     unit of each fixed problem, extrapolated per unit to the whole problem:
-    one image of C1 / C3a / C3b, one (batch, head) pair of C4."""
+    one image of C1 / C3a / C3b / C5, one (batch, head) pair of C4, one
+    (batch, key/value head) unit of the decode."""
     import numpy as np
 
     from oracle import oracle as orc
@@ -459,8 +460,38 @@ def cpu_baseline_ops() -> dict:
     dt = timed(lambda: orc.attention(q, kk, v, None, None, 0, threads))
     out["attention_bf16_causal_c4"] = {"tflops": 4 * 128 * 4096 * 4097 // 2 / dt / 1e12,
                                        "sample": "1 of 256 (batch, head) pairs, f64 dense attention"}
+    # decode: one (batch, key/value head) unit of the 8 x 32/8 heads x 8192 keys problem
+    q = rng.standard_normal((1, 4, 1, 128)).astype(np.float32)
+    kk, v = (rng.standard_normal((1, 1, 8192, 128)).astype(np.float32) for _ in range(2))
+    dt = timed(lambda: orc.attention(q, kk, v, None, None, None, threads))
+    out["attention_bf16_decode_gqa"] = {"tflops": 4 * 4 * 8192 * 128 / dt / 1e12,
+                                        "gbs": 2 * 8192 * 128 * 2 / dt / 1e9,
+                                        "sample": "1 of 64 (batch, key/value head) units, f64 dense attention; "
+                                                  "GB/s counts the unit's K/V at 2 bytes per value"}
+    # C5: one image through the encoder chain composed from the oracle's operators
+    from forma_b200.vit import ViTConfig
+    from oracle import vit as ovit
+
+    cfg = ViTConfig()
+    E, M, C, P = cfg.embed, cfg.mlp, cfg.channels, cfg.patch
+    sd = 1.0 / math.sqrt(E)
+    blocks = [{"qkv": rng.standard_normal((3 * E, E, 1, 1)) * sd, "proj": rng.standard_normal((E, E, 1, 1)) * sd,
+               "fc1": rng.standard_normal((M, E, 1, 1)) * sd,
+               "fc2": rng.standard_normal((E, M, 1, 1)) / math.sqrt(M)}]  # one of the 12 layers
+    img = rng.standard_normal((1, C, cfg.image, cfg.image))
+    wp = rng.standard_normal((E, C, P, P)) / math.sqrt(C * P * P)
+    pos, cls = rng.standard_normal((1, cfg.tokens, E)) * 0.02, rng.standard_normal((1, 1, E)) * 0.02
+    dt = timed(lambda: ovit.forward(img, wp, pos, cls, blocks, cfg.heads, P, cfg.eps, nthreads=threads))
+    fl = cfg.flops()
+    one = (fl["patch"] + (fl["total"] - fl["patch"]) / cfg.layers) / cfg.batch  # patch conv + one layer, one image
+    out["vit_encoder_c5"] = {"tflops": one / dt / 1e12,
+                             "sample": "1 of 64 images, the patch convolution and 1 of 12 layers, through the encoder "
+                                       "composed from the oracle (f64 convolution, attention and layer norm; "
+                                       "projections as f64 matrix products)"}
     for v_ in out.values():
         v_["tflops"] = round(v_["tflops"], 5)
+        if "gbs" in v_:
+            v_["gbs"] = round(v_["gbs"], 3)
         v_.update({"cores": threads, "kind": "port", "extrapolated": True})
     return out
 
@@ -787,7 +818,7 @@ def main(argv=None) -> int:
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--profile", default=None,
                     help="run one workload --steps times and exit (conv_c3a, conv_c3b, attn_c4, attn_c4_small, vit_c5, "
-                         "c5_qkv, c5_fc1, "
+                         "c5_qkv, c5_fc1, decode_gqa, "
                          "rows_max_argmax_moments, "
                          "conv_c1, rows_softmax, rows_argmax, rows_moments)")
     args = ap.parse_args(argv)

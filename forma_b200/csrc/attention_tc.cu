@@ -1409,11 +1409,11 @@ int launch_decode16(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const
     if (!rows16(ql) || !rows16(kl) || !rows16(vl)) return FB_ERR_UNSUPPORTED;
     if (Lk > 0x7fffffffull || ql.batch * H * L > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
     const uint64_t B = ql.batch, units = B * Hkv;
-    // Key ranges: about two CTAs (of four warps) per SM, at least 256 keys
-    // per warp; `splits` CTAs per (batch, key/value head), each leaving one
-    // record per query row.
+    // Key ranges: about two CTAs (of four warps) per SM, at least 64 keys per
+    // warp (few units, e.g. one batch per GPU, still fill the GPU); `splits`
+    // CTAs per (batch, key/value head), each leaving one record per query row.
     const uint64_t target = (uint64_t)sm_count() * 2;
-    const uint64_t want = std::max<uint64_t>(1, std::min<uint64_t>(target / units, (Lk + 256 * DEC_WARPS - 1) / (256 * DEC_WARPS)));
+    const uint64_t want = std::max<uint64_t>(1, std::min<uint64_t>(target / units, (Lk + 64 * DEC_WARPS - 1) / (64 * DEC_WARPS)));
     const uint64_t kps = ((Lk + want * DEC_WARPS - 1) / (want * DEC_WARPS) + 15) / 16 * 16;  // keys per warp
     const uint64_t splits = (Lk + kps * DEC_WARPS - 1) / (kps * DEC_WARPS);
     const uint64_t bytes = B * H * L * splits * (D + 2) * sizeof(float);

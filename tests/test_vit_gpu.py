@@ -13,51 +13,19 @@ from forma_b200 import api
 from forma_b200.api import ConvOptions
 from forma_b200.vit import ViTConfig, ViTEncoder
 from oracle import oracle as orc
+from oracle import vit as ovit
+from oracle.vit import f32, gelu_tanh, low  # noqa: F401  (the chain's rounding points; other tests import them here)
 
 pytestmark = pytest.mark.gpu
 
 
-def low(x):
-    """Nearest-even rounding to BF16 and back (the casts of the chain)."""
-    return orc.decode_bits(orc.round_bits(np.asarray(x, np.float32), "bf16"), "bf16").astype(np.float64)
-
-
-def gelu_tanh(x):
-    # tensor-core/src/host_tensor/activation.rs:9-20, in f64
-    return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
-
-
-def f32(x):
-    return np.asarray(x, np.float64).astype(np.float32).astype(np.float64)
-
-
 def oracle_forward(enc: ViTEncoder, img: torch.Tensor) -> np.ndarray:
+    """The oracle composition (oracle/vit.py) on the encoder's weights."""
     cfg = enc.cfg
-    B, L, E, H, D = img.shape[0], cfg.tokens, cfg.embed, cfg.heads, cfg.head_dim
-    w = lambda t: t.float().cpu().numpy().astype(np.float64)
-    p = cfg.patch
-    pt = orc.conv(w(img), w(enc.w_patch), [p, p], [1, 1], [0, 0], [0, 0], nthreads=orc.threads())
-    patches = f32(pt.reshape(B, E, -1).transpose(0, 2, 1))                     # [B, P, E] f32 conv result
-    pos, cls = w(enc.pos), w(enc.cls)
-    x = np.concatenate([np.broadcast_to(f32(cls + pos[:, :1]), (B, 1, E)), f32(patches + pos[:, 1:])], axis=1)
-
-    def norm(t):
-        return orc.row_stats(t.reshape(-1, E).astype(np.float32), cfg.eps, which=("norm",))["norm"].astype(
-            np.float64).reshape(t.shape)
-
-    def proj(t, weight):
-        return f32(t @ w(weight)[:, :, 0, 0].T)
-
-    for blk in enc.blocks:
-        h = low(norm(x))
-        qkv = proj(h, blk["qkv"]).reshape(B, L, 3, H, D)
-        q, k, v = (low(qkv[:, :, i].transpose(0, 2, 1, 3)) for i in range(3))
-        a = orc.attention(q, k, v, nthreads=orc.threads())
-        a_low = low(np.asarray(a, np.float64).transpose(0, 2, 1, 3).reshape(B, L, E))
-        x = f32(x + proj(a_low, blk["proj"]))
-        m = proj(low(norm(x)), blk["fc1"])
-        x = f32(x + proj(low(gelu_tanh(m)), blk["fc2"]))
-    return x
+    w = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    blocks = [{k: w(blk[k]) for k in ("qkv", "proj", "fc1", "fc2")} for blk in enc.blocks]
+    return ovit.forward(w(img), w(enc.w_patch), w(enc.pos), w(enc.cls), blocks, cfg.heads, cfg.patch, cfg.eps,
+                        nthreads=orc.threads())
 
 
 def test_vit_chain_small_matches_oracle(cuda):
