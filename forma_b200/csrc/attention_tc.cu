@@ -1130,7 +1130,20 @@ struct Dec16Params {
     float scale_log2, shift;
     int32_t causal, causal_offset;
     float* part;  // records [((batch * H + head) * L + query) * splits + range] x {base, l, O[D]}
+    // cluster != 0: a unit's `splits` CTAs form one thread-block cluster and
+    // merge their records through distributed shared memory, each writing some
+    // of the output rows (no records in global memory, no merge launch)
+    uint32_t cluster;
+    void* out;
+    uint32_t out_low;           // 0: f32 rows; FB_BF16 / FB_F16: rounded once (nearest even)
+    uint64_t o_sb, o_sh, o_sl;  // output strides (elements of the output type)
 };
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 
 template <int FMT>
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -1366,6 +1379,9 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) attn_decode16_kernel(Dec16Para
         }
     }
     __syncthreads();
+    // the CTA's records: global memory, or (cluster) the upper half of warp
+    // 0's ring, clear of every warp's {m, l, O} area
+    float* cmb = reinterpret_cast<float*>(dsm) + DEC_STAGES * STAGE * 2;
     for (uint32_t r = 0; r < R; ++r) {
         float mw[DEC_WARPS], lw[DEC_WARPS], M = NEG;
 #pragma unroll
@@ -1381,7 +1397,8 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) attn_decode16_kernel(Dec16Para
             Lr = fmaf(lw[w], wt[w], Lr);
         }
         const uint32_t h = hkv * p.G + r / p.L, q = r % p.L;
-        float* rec = p.part + ((((uint64_t)b * p.H + h) * p.L + q) * p.splits + split) * (D + 2);
+        float* rec = p.cluster ? cmb + r * (D + 2)
+                               : p.part + ((((uint64_t)b * p.H + h) * p.L + q) * p.splits + split) * (D + 2);
         if (threadIdx.x == 0) {
             rec[0] = M == NEG ? 0.0f : M + p.shift;
             rec[1] = Lr;
@@ -1394,6 +1411,42 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) attn_decode16_kernel(Dec16Para
                     acc = fmaf(reinterpret_cast<const float*>(dsm + (size_t)w * DEC_STAGES * STAGE)[r * (D + 2) + 2 + d], wt[w], acc);
             rec[2 + d] = acc;
         }
+    }
+    if (p.cluster) {
+        // The cluster's CTAs combine its records as attn_merge_kernel does
+        // (ranges in index order, the same arithmetic), CTA t taking rows
+        // t, t + splits, ...
+        cluster_sync();  // every CTA's records are in its shared memory
+        {
+            const uint32_t cmb_s = (uint32_t)__cvta_generic_to_shared(cmb);
+            for (uint32_t r = split; r < R; r += p.splits) {
+                float Mx = NEG;
+                for (uint32_t t = 0; t < p.splits; ++t) {
+                    const uint32_t rec = mapa_u32(cmb_s + r * (D + 2) * 4, t);
+                    if (ld_cluster_f32(rec + 4) > 0.0f) Mx = fmaxf(Mx, ld_cluster_f32(rec));
+                }
+                float Lr = 0.0f, acc = 0.0f;
+                const uint32_t d = threadIdx.x;  // one output column per thread (D <= 128)
+                for (uint32_t t = 0; t < p.splits; ++t) {
+                    const uint32_t rec = mapa_u32(cmb_s + r * (D + 2) * 4, t);
+                    const float lt = ld_cluster_f32(rec + 4);
+                    if (!(lt > 0.0f)) continue;
+                    const float wgt = exp2f(ld_cluster_f32(rec) - Mx);
+                    Lr = fmaf(lt, wgt, Lr);
+                    if (d < (uint32_t)D) acc = fmaf(ld_cluster_f32(rec + (2 + d) * 4), wgt, acc);
+                }
+                const float inv = Lr > 0.0f ? 1.0f / Lr : 0.0f;
+                const uint32_t h = hkv * p.G + r / p.L, q = r % p.L;
+                const uint64_t off = (uint64_t)b * p.o_sb + (uint64_t)h * p.o_sh + (uint64_t)q * p.o_sl + d;
+                if (d < (uint32_t)D) {
+                    if (p.out_low)
+                        static_cast<uint16_t*>(p.out)[off] = p.out_low == FB_BF16 ? encode_bf16(acc * inv) : encode_f16(acc * inv);
+                    else
+                        static_cast<float*>(p.out)[off] = acc * inv;
+                }
+            }
+        }
+        cluster_sync();  // the records stay in shared memory until every CTA has read them
     }
 }
 
@@ -1416,11 +1469,16 @@ int launch_decode16(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const
     const uint64_t want = std::max<uint64_t>(1, std::min<uint64_t>(target / units, (Lk + 64 * DEC_WARPS - 1) / (64 * DEC_WARPS)));
     const uint64_t kps = ((Lk + want * DEC_WARPS - 1) / (want * DEC_WARPS) + 15) / 16 * 16;  // keys per warp
     const uint64_t splits = (Lk + kps * DEC_WARPS - 1) / (kps * DEC_WARPS);
-    const uint64_t bytes = B * H * L * splits * (D + 2) * sizeof(float);
-    float* part = static_cast<float*>(scratch(st, bytes, SCRATCH_ATTN_SPLIT));
-    if (!part) {  // none (e.g. first use inside a graph capture): the tile kernel takes it
-        (void)cudaGetLastError();
-        return FB_ERR_UNSUPPORTED;
+    // At most eight ranges: one cluster per unit merges in shared memory.
+    const bool cluster = splits <= 8;
+    float* part = nullptr;
+    if (!cluster) {
+        const uint64_t bytes = B * H * L * splits * (D + 2) * sizeof(float);
+        part = static_cast<float*>(scratch(st, bytes, SCRATCH_ATTN_SPLIT));
+        if (!part) {  // none (e.g. first use inside a graph capture): the tile kernel takes it
+            (void)cudaGetLastError();
+            return FB_ERR_UNSUPPORTED;
+        }
     }
     Dec16Params d{};
     d.q = static_cast<const uint16_t*>(a.q) + a.q_offset;
@@ -1436,12 +1494,34 @@ int launch_decode16(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const
     d.causal = a.causal ? 1 : 0;
     d.causal_offset = a.causal_offset;
     d.part = part;
+    d.cluster = cluster ? 1 : 0;
+    d.out = a.out_low ? static_cast<void*>(reinterpret_cast<uint16_t*>(a.out) + a.o_offset)
+                      : static_cast<void*>(a.out + a.o_offset);
+    d.out_low = a.out_low;
+    d.o_sb = ol.s_batch, d.o_sh = ol.s_head, d.o_sl = ol.s_row;
     const uint64_t grid = units * splits;
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
     const int smem = DEC_WARPS * DEC_STAGES * 2 * 16 * D * 2;  // bytes of the per-warp rings
     auto kernel = fmt ? attn_decode16_kernel<D, 1> : attn_decode16_kernel<D, 0>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return launch_status("shared-memory attribute");
+    if (cluster) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(32 * DEC_WARPS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)splits;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kernel, d) != cudaSuccess) return launch_status("kernel launch");
+        count_launch(kernel_name("attn_decode16_kernel", {D, (int)fmt}).c_str());
+        return launch_status("kernel launch");
+    }
     kernel<<<(unsigned)grid, 32 * DEC_WARPS, smem, st>>>(d);
     count_launch(kernel_name("attn_decode16_kernel", {D, (int)fmt}).c_str());
     if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
