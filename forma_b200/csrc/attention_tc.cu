@@ -30,7 +30,10 @@
 //               path and normalises exactly the weights used).  The running
 //               max is only raised (and O rescaled in TMEM) when a row max
 //               exceeds it by more than 2^8, so P <= 2^8 and rescales are rare.
-//               Finally O / l is written as f32.
+//               Finally O / l: staged in the idle K/V ring once both tiles'
+//               MMAs are done and written by TMA tensor stores (rows past L
+//               clipped by the map), or stored row by row where the output
+//               has no tensor map or the key range is split.
 // Ordering: a tcgen05.commit completes only after every earlier MMA of the
 // issuing thread, so "S_t of tile j+1 ready" also certifies that PV_t of tile
 // j has consumed P_t and updated O_t: the softmax needs no other wait.
@@ -83,6 +86,7 @@ struct AttnParams {
     uint32_t rec_rows;      // record rows per (batch, head): the query rows L
     uint32_t q_mod;         // a row's query index is row % q_mod (GQA-packed rows; L otherwise)
     float* part;
+    uint32_t tma_out;       // 1: output rows staged in the K/V ring and written by TMA tensor stores (splits == 1)
 };
 
 // First element of output row (batch, head, q) when the rows are 16-bit.
@@ -197,7 +201,8 @@ __device__ __forceinline__ uint32_t visible_tiles(const AttnParams& p, uint32_t 
 template <int D, int MASK, int QT>
 __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
-                                                              const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+                                                              const __grid_constant__ CUtensorMap tmV,
+                                                              const __grid_constant__ CUtensorMap tmO, AttnParams p) {
     using C = ACfg<D, QT>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -517,6 +522,67 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
         }
         // epilogue: O / l, f32 rows
         if (ok && n > 0 && !__all_sync(0xffffffffu, mbar_wait(&o_done[t], 0))) ok = false;
+        if (p.tma_out) {
+            // Staged epilogue: once every MMA of both tiles has completed, the
+            // K/V ring is idle; each thread writes its row of O / l there in
+            // the 128-byte-swizzled boxes of the output's tensor map (128 rows
+            // x 128 bytes each), and one thread writes the boxes by TMA tensor
+            // stores instead of every thread storing its own row.
+#pragma unroll
+            for (int tt = 0; tt < QT; ++tt)
+                if (tt != t && n_t[tt] > 0 && ok && !__all_sync(0xffffffffu, mbar_wait(&o_done[tt], 0))) ok = false;
+            if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
+            tc_fence_after();
+            const bool load = ok && n > 0;
+            const float inv = (load && l > 0.0f) ? 1.0f / l : 0.0f;
+            const uint32_t esz = p.out_low ? 2u : 4u;
+            unsigned char* stage = sKV + (uint32_t)t * (TQ * D * esz);
+            const uint32_t swz = row & 7u;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                if (load) {
+                    tmem_ld32(tmem + lane_base + C::o_col(t) + c * 32, r);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = 0u;
+                }
+                if (p.out_low) {  // boxes of 64 16-bit values: chunk c is half of box c / 2
+                    unsigned char* dst = stage + (c / 2) * (TQ * 128) + row * 128;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t j = (uint32_t)((c % 2) * 4 + i);
+                        *reinterpret_cast<uint4*>(dst + ((j ^ swz) * 16)) = make_uint4(
+                            encode_low_pair(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv, p.out_low),
+                            encode_low_pair(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv, p.out_low));
+                    }
+                } else {  // boxes of 32 f32 values
+                    unsigned char* dst = stage + c * (TQ * 128) + row * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(dst + ((j ^ swz) * 16)) =
+                            make_float4(__uint_as_float(r[4 * j]) * inv, __uint_as_float(r[4 * j + 1]) * inv,
+                                        __uint_as_float(r[4 * j + 2]) * inv, __uint_as_float(r[4 * j + 3]) * inv);
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();  // the staged rows are visible to the TMA store
+            asm volatile("bar.sync 1, %0;" ::"r"(QT * 128) : "memory");  // every softmax warp's rows are staged
+            if (warp == 2 && lane == 0) {
+                const int boxes = p.out_low ? D / 64 : D / 32;
+                for (int tt = 0; tt < QT; ++tt) {
+                    if (q0 + tt * TQ >= p.L) continue;
+                    for (int bx = 0; bx < boxes; ++bx)
+                        tma_store_4d(&tmO, bx * (p.out_low ? 64 : 32), (int32_t)(q0 + tt * TQ), (int32_t)head,
+                                     (int32_t)batch, sKV + tt * (TQ * D * esz) + bx * (TQ * 128));
+                }
+                bulk_commit_group();
+                bulk_wait_read_all();  // shared memory stays valid until the stores have read it
+            }
+        } else {
         if (!ok) atomicOr(&g_attn_status, 1u << DEV_ATTN_TIMEOUT);
         tc_fence_after();
         // `ok` and n are warp-uniform, so the loads are too; only the stores
@@ -569,6 +635,7 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
             }
         }
         tc_fence_before();
+        }
     }
     __syncthreads();
     if (warp == 1) {
@@ -997,6 +1064,8 @@ bool make_rows_map(CUtensorMap* map, const void* ptr, uint32_t fmt, uint64_t D, 
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_out_map(CUtensorMap* map, void* ptr, uint32_t out_low, uint64_t D, const RowsLayout& l);
+
 // L rows per head over H heads sharing Hkv key/value heads; q_mod < L when
 // a GQA group's heads are packed into the rows of one head (row % q_mod is
 // the query index).
@@ -1077,7 +1146,10 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
         }
     }
     if (grid > 0x7fffffffull) return FB_ERR_UNSUPPORTED;
-    kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
+    // whole ranges: the output through a TMA map where its layout allows one
+    CUtensorMap to{};
+    p.tma_out = p.splits == 1 && make_out_map(&to, p.out, p.out_low, D, ol) ? 1u : 0u;
+    kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, to, p);
     count_launch(kernel_name("attn_fwd_kernel", {D, (int)a.mask_kind, QT}).c_str());
     if (p.splits > 1) {
         if (cudaGetLastError() != cudaSuccess) return launch_status("kernel launch");
