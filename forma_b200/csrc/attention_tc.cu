@@ -262,6 +262,26 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
         }
         mbar_init(drain, 1);
         fence_barrier_init();
+        // The producer is this thread: the Q tiles and the first ring's K/V
+        // (whose slots are free) load while TMEM is allocated and the block
+        // synchronises.
+        if (n_kv > 0) {
+            mbar_arrive_expect_tx(q_full, QT * C::Q_BYTES);
+            for (int t = 0; t < QT; ++t)
+                for (int b = 0; b < C::BOXES; ++b)
+                    tma_load_4d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, (int32_t)(q0 + t * TQ), (int32_t)head,
+                                (int32_t)batch, q_full);
+        }
+        for (uint32_t j = 0; j < n_kv && j < (uint32_t)C::STAGES; ++j) {
+            unsigned char* kd = sKV + j * C::STAGE_BYTES;
+            mbar_arrive_expect_tx(&k_full[j], C::K_BYTES);
+            for (int b = 0; b < C::BOXES; ++b)
+                tma_load_4d(kd + b * (TK * 128), &tmK, b * 64, (int32_t)((j0 + j) * TK), kv_head, k_b, &k_full[j]);
+            mbar_arrive_expect_tx(&v_full[j], C::V_BYTES);
+            for (int b = 0; b < C::BOXES; ++b)
+                tma_load_4d(kd + C::K_BYTES + b * (TK * 128), &tmV, b * 64, (int32_t)((j0 + j) * TK), kv_head, v_b,
+                            &v_full[j]);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -274,19 +294,14 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ TMA producer
-        if (n_kv > 0) {
-            mbar_arrive_expect_tx(q_full, QT * C::Q_BYTES);
-            for (int t = 0; t < QT; ++t)
-                for (int b = 0; b < C::BOXES; ++b)
-                    tma_load_4d(sQ + t * C::Q_BYTES + b * (TQ * 128), &tmQ, b * 64, (int32_t)(q0 + t * TQ), (int32_t)head,
-                                (int32_t)batch, q_full);
-        }
         // K and V have their own slots and barriers: K(j) is released once
         // both tiles' S(j) are computed, a key step before V(j), so the
-        // next K tiles load two key steps ahead of their use.
-        uint32_t issued_k = 0, issued_v = 0;
+        // next K tiles load two key steps ahead of their use.  The first
+        // STAGES key tiles were issued before the block barrier.
+        const uint32_t pre = n_kv < (uint32_t)C::STAGES ? n_kv : (uint32_t)C::STAGES;
+        uint32_t issued_k = pre, issued_v = pre;
         bool failed = false;
-        for (uint32_t j = 0; j < n_kv; ++j) {
+        for (uint32_t j = pre; j < n_kv; ++j) {
             const uint32_t s = j % C::STAGES, ph = ((j / C::STAGES) & 1) ^ 1;
             unsigned char* kd = sKV + s * C::STAGE_BYTES;
             unsigned char* vd = kd + C::K_BYTES;
