@@ -103,3 +103,43 @@ def test_decode_tensor_core_key_split(cuda, lq, lk, causal, depth):
     err = np.abs(a - exp).max() / max(np.abs(exp).max(), 1e-30)
     assert err <= 2e-2, err
     assert err <= 3e-3, err  # BF16 P, f32 accumulation and merge
+
+
+def _decode16(cuda, qs, ks, causal=None, dtype=torch.bfloat16, seed=40, out_low=False):
+    # 16-bit inputs (nearest-even conversion); the oracle sees their exact values
+    lows = [torch.from_numpy(rnd(s, seed + i)).to(dtype) for i, s in enumerate((qs, ks, ks))]
+    q, k, v = (t.float().numpy() for t in lows)
+    tq, tk, tv = (t.to(cuda) for t in lows)
+    opts = AttentionOptions(causal=causal)
+    got = api.attention_low(tq, tk, tv, None, opts) if out_low else api.attention_low_f32(tq, tk, tv, None, opts)
+    route = api.last_route()
+    assert api.device_status() == 0
+    exp = orc.attention(q, k, v, causal=causal, nthreads=orc.threads())
+    a = got.float().cpu().numpy().astype(np.float64)
+    err = np.abs(a - exp).max() / max(np.abs(exp).max(), 1e-30)
+    assert err <= 2e-2, err  # bf16 tensor-core gate
+    assert err <= (8e-3 if out_low else 3e-3), err  # the kernel's own accuracy (16-bit P, f32 accumulation)
+    return route
+
+
+@pytest.mark.parametrize("case", ["bench_gqa", "bench_gqa_one_batch", "rows16_causal", "d64_mha_f16", "low_out"])
+def test_decode16_kernel_routes(cuda, case):
+    """16-bit decode with at most 16 query rows per key/value head runs on
+    attn_decode16_kernel: 40 (batch, key/value head) units of the bench's
+    GQA group (each unit's seven key ranges one cluster merging in shared
+    memory: one launch), a single batch (more than eight ranges: records
+    merged by attn_merge_kernel), 16 rows per head with causal offsets,
+    depth 64 with f16 and one head per group, and a 16-bit output rounded
+    in the cluster merge."""
+    dec128 = ["attn_decode16_kernel<128,1>"]
+    if case == "bench_gqa":
+        assert _decode16(cuda, (5, 32, 1, 128), (5, 8, 4096, 128)) == dec128
+    elif case == "bench_gqa_one_batch":
+        route = _decode16(cuda, (1, 32, 1, 128), (1, 8, 8192, 128))
+        assert route == dec128 + ["attn_merge_kernel<128>"], route
+    elif case == "rows16_causal":
+        assert _decode16(cuda, (2, 8, 4, 128), (2, 2, 4100, 128), causal=4096)[0] == dec128[0]
+    elif case == "d64_mha_f16":
+        assert _decode16(cuda, (2, 4, 2, 64), (2, 4, 3000, 64), dtype=torch.float16)[0] == "attn_decode16_kernel<64,0>"
+    else:
+        assert _decode16(cuda, (5, 32, 1, 128), (5, 8, 4096, 128), out_low=True) == dec128
