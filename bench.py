@@ -286,11 +286,13 @@ def _flush_l2(buf):
     buf.add_(1)  # 256 MB written between timed launches: larger than the 126 MB L2
 
 
-def time_op(torch, fn, iters, flush_buf, stream):
-    """Average device time of fn over `iters` launches, L2 flushed before each."""
+def time_op(torch, fn, iters, flush_buf, stream, flush=True):
+    """Average device time of fn over `iters` launches, L2 flushed before each
+    (flush=False: the call streams inputs larger than L2 itself)."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
     for a, b in evs:
-        _flush_l2(flush_buf)
+        if flush:
+            _flush_l2(flush_buf)
         a.record(stream)
         fn()
         b.record(stream)
@@ -321,20 +323,30 @@ def run_ops(api, dev, dist, args, pk) -> dict:
         b, e = shard_range(total, dist.world, dist.rank)
         return b, e, e - b
 
-    def record(name, fn, flops, peak, peak_name, note=None, nbytes=None, shard=None):
+    L2_BYTES = 126 * 1024 * 1024
+
+    def record(name, fn, flops, peak, peak_name, note=None, nbytes=None, shard=None, in_bytes=0):
         """`flops` / `nbytes`: the whole fixed problem's algorithmic FLOPs and
         HBM bytes (inputs read once, outputs written once); the time is the
-        slowest rank's, so the rate is the job's."""
+        slowest rank's, so the rate is the job's.  `in_bytes`: the bytes this
+        rank's call streams in; at least twice L2 on every rank and the calls
+        are timed back to back (each call evicts its own inputs), otherwise L2
+        is flushed by a 256 MB write before each call.  (Given only for calls
+        whose outputs are small next to their inputs: a large output leaves
+        dirty lines in L2 for the next call to write back, as the flush does.)"""
         for _ in range(2):
             fn()
         torch.cuda.synchronize(dev)
         dist.barrier()
-        ms = dist.max(time_op(torch, fn, iters, flush, stream))
+        no_flush = dist.max(0.0 if in_bytes >= 2 * L2_BYTES else 1.0) == 0.0  # the same choice on every rank
+        ms = dist.max(time_op(torch, fn, iters, flush, stream, flush=not no_flush))
         tf = flops / (ms / 1e3) / 1e12
         res[name] = {"tflops": round(tf, 2), "ms": round(ms, 4), "flop_per_call": flops,
                      "roofline_frac": round(tf / peak / dist.world, 4), "peak_tflops": round(peak, 1),
                      "peak": peak_name + (f" per GPU, x{dist.world} GPUs" if dist.world > 1 else ""),
-                     "scaling": "strong", "shard": shard}
+                     "scaling": "strong", "shard": shard,
+                     "l2": (f"inputs larger than L2 ({in_bytes / 2**20:.0f} MiB per call on this rank), no flush"
+                            if no_flush else "L2 flushed by a 256 MB write before each call")}
         if nbytes:
             gbs = nbytes / (ms / 1e3) / 1e9
             res[name].update({"bytes_per_call": nbytes, "hbm_gbs": round(gbs, 1),
@@ -378,7 +390,7 @@ def run_ops(api, dev, dist, args, pk) -> dict:
     record("attention_bf16_causal_c4", lambda: api.attention_low_f32_into(q, k, v, None, AttentionOptions(causal=0), o4),
            4 * 8 * 32 * 128 * L * (L + 1) // 2, pk["bf16_tflops"], "measured bf16 dense (burst)",
            "causal FLOPs count the diagonal: 4*B*H*D*L(L+1)/2", nbytes=8 * 32 * L * 128 * (3 * 2 + 4),
-           shard=f"(batch, head) pairs {p0}:{p1} of 256 on this rank")
+           shard=f"(batch, head) pairs {p0}:{p1} of 256 on this rank", in_bytes=n * L * 128 * 2 * 3)
     del q, k, v, o4
     # decode: one query per head, 32 query heads over 8 key/value heads, 8192 keys, bf16 (HBM-bound:
     # reads K and V once); batches sharded
@@ -391,7 +403,8 @@ def run_ops(api, dev, dist, args, pk) -> dict:
            4 * 8 * 32 * 1 * 8192 * 128, pk["bf16_tflops"], "measured bf16 dense (burst)",
            "the 4 query heads of a key/value head as one 16-row block on the warp-level MMA, K/V streamed once "
            "through per-warp cp.async rings, key ranges merged on the device",
-           nbytes=2 * 8 * 8 * 8192 * 128 * 2 + 8 * 32 * 128 * 2 + 8 * 32 * 128 * 4, shard=f"batches {b0}:{b1} of 8")
+           nbytes=2 * 8 * 8 * 8192 * 128 * 2 + 8 * 32 * 128 * 2 + 8 * 32 * 128 * 4, shard=f"batches {b0}:{b1} of 8",
+           in_bytes=n * 8 * 8192 * 128 * 2 * 2)
     del q, k, v
     # low-precision GEMM (the reference's cuBLAS matmul_low_f32): [8192, 8192] x [8192, 8192] bf16, f32
     # output, rows of the left operand sharded
