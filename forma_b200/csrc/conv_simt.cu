@@ -118,21 +118,33 @@ __global__ void __launch_bounds__(T_THREADS) conv2d_f32_tiled_kernel(ConvArgs a)
         for (int j = 0; j < T_TP; ++j) acc[i][j] = 0.0f;
 
     const float* in_n = in + a.in_offset + (uint64_t)n * a.in_stride_n + (uint64_t)group * cpg * a.in_stride_c;
+    // Staging without per-element index division: each thread keeps one
+    // input column (lanes 0 .. IN_C - 1 of each warp) and walks the (channel,
+    // row) pairs of its warp with a pointer step; the weights are read as
+    // each output channel's contiguous run of (channel, tap) values.
+    constexpr int SW = T_THREADS / 32;               // warps staging the input
+    const int scol = tid & 31, swarp = tid >> 5;
+    const int sx = c0 + scol - pad_w;
+    const bool col_ok = scol < IN_C && sx >= 0 && sx < W;
+    const int wo = tid % T_OC, wk0 = tid / T_OC;   // weight: output channel, first (channel x tap) index
+    const float* w_o = w + a.w_offset + (uint64_t)(oc0 + wo) * a.w_stride_o;
     for (int cb = 0; cb < cpg; cb += T_CCH) {
         const int cn = min(T_CCH, cpg - cb);
-        for (int i = tid; i < T_CCH * IN_R * IN_C; i += T_THREADS) {
-            const int cc = i / (IN_R * IN_C), rr = (i / IN_C) % IN_R, col = i % IN_C;
-            const int y = r0 + rr - pad_h, x = c0 + col - pad_w;
-            float v = 0.0f;
-            if (cc < cn && y >= 0 && y < H && x >= 0 && x < W)
-                v = __ldg(in_n + (uint64_t)(cb + cc) * a.in_stride_c + (uint64_t)y * W + x);
-            s_in[cc][rr][col] = v;
+        if (scol < IN_C) {
+            for (int rr = swarp; rr < IN_R; rr += SW) {
+                const int y = r0 + rr - pad_h;
+                const bool ok = col_ok && y >= 0 && y < H;
+                const float* src = in_n + (uint64_t)cb * a.in_stride_c + (uint64_t)(ok ? y : 0) * W + (ok ? sx : 0);
+#pragma unroll 4
+                for (int cc = 0; cc < T_CCH; ++cc) {
+                    s_in[cc][rr][scol] = (ok && cc < cn) ? __ldg(src) : 0.0f;
+                    src += a.in_stride_c;
+                }
+            }
         }
-        for (int i = tid; i < T_CCH * KH * KW * T_OC; i += T_THREADS) {
-            const int o = i % T_OC, tap = (i / T_OC) % (KH * KW), cc = i / (T_OC * KH * KW);
-            float v = 0.0f;
-            if (cc < cn) v = __ldg(w + a.w_offset + (uint64_t)(oc0 + o) * a.w_stride_o + (uint64_t)(cb + cc) * a.w_stride_c + tap);
-            s_w[cc][tap][o] = v;
+        for (int k = wk0; k < T_CCH * KH * KW; k += T_THREADS / T_OC) {
+            const int cc = k / (KH * KW), tap = k - cc * (KH * KW);
+            s_w[cc][tap][wo] = cc < cn ? __ldg(w_o + (uint64_t)(cb + cc) * a.w_stride_c + tap) : 0.0f;
         }
         __syncthreads();
         for (int cc = 0; cc < cn; ++cc) {
