@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(T_THREADS) conv2d_f32_tiled_kernel(ConvArgs a)
     const int scol = tid & 31, swarp = tid >> 5;
     const int sx = c0 + scol - pad_w;
     const bool col_ok = scol < IN_C && sx >= 0 && sx < W;
-    const int wo = tid % T_OC, wk0 = tid / T_OC;   // weight: output channel, first (channel x tap) index
+    const int wo = tid % T_OC, wc0 = tid / T_OC;   // weight: output channel, first input channel
     const float* w_o = w + a.w_offset + (uint64_t)(oc0 + wo) * a.w_stride_o;
     for (int cb = 0; cb < cpg; cb += T_CCH) {
         const int cn = min(T_CCH, cpg - cb);
@@ -142,9 +142,10 @@ __global__ void __launch_bounds__(T_THREADS) conv2d_f32_tiled_kernel(ConvArgs a)
                 }
             }
         }
-        for (int k = wk0; k < T_CCH * KH * KW; k += T_THREADS / T_OC) {
-            const int cc = k / (KH * KW), tap = k - cc * (KH * KW);
-            s_w[cc][tap][wo] = cc < cn ? __ldg(w_o + (uint64_t)(cb + cc) * a.w_stride_c + tap) : 0.0f;
+        for (int cc = wc0; cc < T_CCH; cc += T_THREADS / T_OC) {
+            const float* src = w_o + (uint64_t)(cb + cc) * a.w_stride_c;
+#pragma unroll
+            for (int tap = 0; tap < KH * KW; ++tap) s_w[cc][tap][wo] = cc < cn ? __ldg(src + tap) : 0.0f;
         }
         __syncthreads();
         for (int cc = 0; cc < cn; ++cc) {
