@@ -779,14 +779,39 @@ __global__ void __launch_bounds__(WARP_ROWS_TB, FULL ? 4 : 1) rows_warp_kernel(R
             const double delta = mean - (double)m32;
             if (var < 0.0) var = 0.0;
             if (op == STREAM_STATS + STATS_LAYER_NORM) {
-                const double inv = 1.0 / sqrt(var + (double)eps);
+                // one f64 reciprocal square root (within an f64 ulp; its f32
+                // rounding is that of the quotient 1 / sqrt but in vanishingly
+                // rare ties)
+                const double inv = rsqrt(var + (double)eps);
                 const float invf = (float)inv, dinv = (float)(delta * inv);
                 auto ln = [&](float x) { return fmaf(x - m32, invf, -dinv); };
+                if (fast && eo.dtype != FB_F32) {
+                    // The accepted sums were finite, so every input and every
+                    // normalised value is finite: one nearest-even pack per
+                    // pair rounds exactly as encode_low_pair does for non-NaN
+                    // values, without its NaN fix-ups.
+                    uint16_t* orow = reinterpret_cast<uint16_t*>(eo.data) + eo.offset + row * eo.row_stride;
+                    const bool bf = eo.dtype == FB_BF16;
 #pragma unroll
-                for (int j = 0; j < NV; ++j)
-                    if (valid(j))
-                        store_row4(eo, row, (lane + (uint64_t)j * 32) * 4,
-                                   make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w)));
+                    for (int j = 0; j < NV; ++j)
+                        if (valid(j)) {
+                            uint32_t w0, w1;
+                            if (bf) {
+                                asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w0) : "f"(ln(c[j].y)), "f"(ln(c[j].x)));
+                                asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w1) : "f"(ln(c[j].w)), "f"(ln(c[j].z)));
+                            } else {
+                                asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w0) : "f"(ln(c[j].y)), "f"(ln(c[j].x)));
+                                asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w1) : "f"(ln(c[j].w)), "f"(ln(c[j].z)));
+                            }
+                            *reinterpret_cast<uint2*>(orow + (lane + (uint64_t)j * 32) * 4) = make_uint2(w0, w1);
+                        }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < NV; ++j)
+                        if (valid(j))
+                            store_row4(eo, row, (lane + (uint64_t)j * 32) * 4,
+                                       make_float4(ln(c[j].x), ln(c[j].y), ln(c[j].z), ln(c[j].w)));
+                }
             } else if (lane == 0) {
                 static_cast<float*>(oa.data)[out_index(oa, row)] = (float)mean;
                 static_cast<float*>(ob.data)[out_index(ob, row)] = (float)var;
