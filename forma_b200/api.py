@@ -649,6 +649,6 @@ def launch_count() -> int:
 
 def last_route() -> list:
     """Kernels the most recent call on this thread enqueued, in launch order
-    (e.g. ``["conv_gemm_pair_kernel<192,8>"]``)."""
+    (e.g. ``["conv_gemm_pair_kernel<192,12>"]``)."""
     r = lib().fb_last_route().decode()
     return r.split(";") if r else []

@@ -352,9 +352,14 @@ __global__ void __launch_bounds__(THREADS, 1) conv_gemm_kernel(const __grid_cons
 // arrive on the even CTA's `tempty`.
 // BN (256 or 192) is the pair tile's N: each CTA loads BN / 2 rows of B, and
 // 192 fits tile counts of N = 768 / 2304 / 3072 to 74 pairs better than 256.
-// EPW epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter,
-// each taking half of the columns) for epilogues with per-element work (the
-// GELU), at one stage less of the ring.
+// EPW epilogue warps: 4 (one per TMEM lane quarter), or for epilogues with
+// per-element work (GELU, 16-bit rounding, the f32 read-modify-write) 8 (two
+// per quarter, each taking half of the columns) on 256-wide tiles and 12
+// (three per quarter, 64 columns each) on 192-wide ones, at one stage less of
+// the ring.  Each epilogue warp's chunk loop is latency-bound (TMEM load,
+// rounding, stores held back by the store queue), so more warps per quarter
+// drain an accumulator sooner: C5's fc1 + GELU 81.9 -> 68.6 us and the C5
+// forward 3.17 -> 2.96 ms going from 8 to 12 (4 warps: fc1 117 us).
 template <int BN_, int EPW = 4>
 struct PairCfg {
     static constexpr int BN = BN_;
@@ -362,13 +367,13 @@ struct PairCfg {
     static constexpr int A_BYTES = BM * BK * 2;      // 16 KB
     static constexpr int B_BYTES = BN / 2 * BK * 2;  // 16 KB (256) / 12 KB (192)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256 ? 6 : 7) - (EPW == 8 ? 1 : 0);
+    static constexpr int STAGES = (BN == 256 ? 6 : 7) - (EPW >= 8 ? 1 : 0);
     static constexpr int TMEM_COLS = 512;            // two BN-column accumulators
     static constexpr int EPI_PITCH = 36;
     static constexpr int EPI_BYTES = EPW * 32 * EPI_PITCH * 4;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
     static_assert(SMEM <= 227 * 1024, "pair configuration exceeds shared memory");
-    static_assert(EPW == 4 || EPW == 8, "four or eight epilogue warps");
+    static_assert(EPW == 4 || EPW == 8 || (EPW == 12 && BN == 192), "four, eight or (192 wide) twelve epilogue warps");
 };
 
 template <int BN_, int EPW>
@@ -885,10 +890,11 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
     const uint64_t N = b.n;
     if (p.m_tiles >= 2) {
         const uint64_t m_pairs = (p.m_tiles + 1) / 2;
-        // Eight epilogue warps (two per TMEM lane quarter) for the epilogues
-        // that do more than store f32 sums: GELU, the read-modify-write add
-        // and the 16-bit rounding, each of which otherwise outlasts a short
-        // (K = 768) main loop; plain f32 stores keep four and the deeper ring.
+        // Eight (256 wide) or twelve (192 wide) epilogue warps for the
+        // epilogues that do more than store f32 sums: GELU, the
+        // read-modify-write add and the 16-bit rounding, each of which
+        // otherwise outlasts a short (K = 768) main loop; plain f32 stores
+        // keep four and the deeper ring.
         const bool heavy_epilogue = p.act || p.accumulate || p.out_low;
         int best = 0;
         uint64_t best_cost = ~0ull;
@@ -896,7 +902,7 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
         for (int bn : {256, 192}) {
             if (N % bn != 0 || (b.mn && bn != 256)) continue;
             const int cl = bn == 256 ? (heavy_epilogue ? pair_clusters<256, 8>() : pair_clusters<256, 4>())
-                                     : (heavy_epilogue ? pair_clusters<192, 8>() : pair_clusters<192, 4>());
+                                     : (heavy_epilogue ? pair_clusters<192, 12>() : pair_clusters<192, 4>());
             if (cl == 0) continue;
             const uint64_t tiles = m_pairs * (N / bn);
             const uint64_t cost = (tiles + cl - 1) / cl * bn;
@@ -931,7 +937,7 @@ int launch_tiles(const CUtensorMap& ta, const BOperand& b, ConvGemmParams p, cud
             p.n_tiles = (uint32_t)(N / best);
             if (heavy_epilogue)
                 return best == 256 ? launch_pair<256, 8>(ta, tb, p, best_clusters, st)
-                                   : launch_pair<192, 8>(ta, tb, p, best_clusters, st);
+                                   : launch_pair<192, 12>(ta, tb, p, best_clusters, st);
             return best == 256 ? launch_pair<256, 4>(ta, tb, p, best_clusters, st)
                                : launch_pair<192, 4>(ta, tb, p, best_clusters, st);
         }

@@ -143,7 +143,7 @@ const char* fb_last_error(void);
 uint64_t fb_launch_count(void);
 /* The kernels that the most recent computing call on this host thread
  * enqueued, separated by ';' in launch order, template instantiations
- * spelled out (e.g. "conv_gemm_pair_kernel<192,8>" or
+ * spelled out (e.g. "conv_gemm_pair_kernel<192,12>" or
  * "attn_fwd_kernel<128,0,2>;attn_merge_kernel<128>"); "" when that call
  * launched nothing.  Shows which route (tensor cores, CUDA cores, split,
  * scratch + cast) served a call.  No counterpart in the reference, whose

@@ -33,7 +33,7 @@ def _rows(m, count, seed):
 def test_c5_projection_gemms_match_oracle(cuda, name, cout, cin):
     """QKV (16-bit output rounded in the epilogue), fc1 (GELU + rounding in the
     epilogue) and the residual projections (f32 read-modify-write epilogue) at
-    M = 12608 tokens, on the CTA-pair kernel with eight epilogue warps and
+    M = 12608 tokens, on the CTA-pair kernel with twelve epilogue warps and
     192-column tiles; 512 sampled rows against f64 products."""
     g = torch.Generator(device="cpu").manual_seed(cout + cin)
     tok = torch.randn(64, 197, cin, generator=g).bfloat16()
@@ -46,7 +46,7 @@ def test_c5_projection_gemms_match_oracle(cuda, name, cout, cin):
         out = torch.empty(64, 1, 197, cout, dtype=torch.bfloat16, device=cuda)
         fn = api.conv_low_into if name == "qkv" else api.conv_low_gelu_into
         fn(x_in, wd, _ONE, out.permute(0, 3, 1, 2))
-        assert api.last_route() == ["conv_gemm_pair_kernel<192,8>"], api.last_route()
+        assert api.last_route() == ["conv_gemm_pair_kernel<192,12>"], api.last_route()
         got = out.view(-1, cout).float().cpu().numpy().astype(np.float64)[rows]
         # the oracle rounds the f64 sum (and GELU) once to BF16; the kernel's
         # f32 sum may sit on the other side of a rounding boundary: one BF16
@@ -59,7 +59,7 @@ def test_c5_projection_gemms_match_oracle(cuda, name, cout, cin):
         base = torch.randn(64, 197, cout, generator=g)
         x = base.to(cuda)
         api.conv_low_f32_accumulate(x_in, wd, _ONE, x.view(64, 1, 197, cout).permute(0, 3, 1, 2))
-        assert api.last_route() == ["conv_gemm_pair_kernel<192,8>"], api.last_route()
+        assert api.last_route() == ["conv_gemm_pair_kernel<192,12>"], api.last_route()
         got = x.view(-1, cout).cpu().numpy().astype(np.float64)[rows]
         want = base.view(-1, cout).double().numpy()[rows] + prod
         err = float(np.abs(got - want).max()) / float(np.abs(want).max())
@@ -107,7 +107,7 @@ def test_c5_layer_kernels_are_the_tensor_core_ones(cuda):
         api._check = orig
     assert api.device_status() == 0
     kinds = {r for route in seen for r in route}
-    assert "conv_gemm_pair_kernel<192,8>" in kinds  # QKV, fc1, proj, fc2
+    assert "conv_gemm_pair_kernel<192,12>" in kinds  # QKV, fc1, proj, fc2
     assert "attn_short_kernel" in kinds
     assert "patches_vec8_kernel" in kinds and "rows_warp_kernel" in kinds
     simt = {"conv_direct_kernel", "attention_simt_kernel", "attention_part_kernel", "gemm_simt_kernel"}
