@@ -87,6 +87,7 @@ struct AttnParams {
     uint32_t q_mod;         // a row's query index is row % q_mod (GQA-packed rows; L otherwise)
     float* part;
     uint32_t tma_out;       // 1: output rows staged in the K/V ring and written by TMA tensor stores (splits == 1)
+    uint32_t tail_qb;       // causal, splits == 1: the lightest query blocks of every head, run last (0: none)
 };
 
 // First element of output row (batch, head, q) when the rows are 16-bit.
@@ -223,10 +224,20 @@ __global__ void __launch_bounds__(ACfg<D, QT>::THREADS, QT == 1 ? 2 : 1) attn_fw
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Consecutive CTAs take the query blocks of one (batch, head), heaviest
     // (last, for causal) first, so the CTAs in flight share a few heads' K/V
-    // in L2.
-    const uint32_t units = p.q_blocks * p.splits;
-    const uint32_t bh = blockIdx.x / units;
-    const uint32_t qb = p.q_blocks - 1 - (blockIdx.x % units) / p.splits;
+    // in L2.  Causal launches hold back each head's `tail_qb` lightest query
+    // blocks and run them last, heaviest first across heads, so the SMs that
+    // finish early pick up short CTAs instead of a late full-length one.
+    const uint32_t lead = (p.q_blocks - p.tail_qb) * p.splits * p.bh;
+    uint32_t bh, qb;
+    if (blockIdx.x < lead) {
+        const uint32_t units = (p.q_blocks - p.tail_qb) * p.splits;
+        bh = blockIdx.x / units;
+        qb = p.q_blocks - 1 - (blockIdx.x % units) / p.splits;
+    } else {  // splits == 1
+        const uint32_t r = blockIdx.x - lead;
+        qb = p.tail_qb - 1 - r / p.bh;
+        bh = r % p.bh;
+    }
     const uint32_t split = blockIdx.x % p.splits;
     const uint32_t j0 = split * p.split_tiles;  // first key tile of this CTA's range
     const uint32_t q0 = qb * (QT * TQ);
@@ -1164,6 +1175,11 @@ int launch_d(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const RowsLa
     // whole ranges: the output through a TMA map where its layout allows one
     CUtensorMap to{};
     p.tma_out = p.splits == 1 && make_out_map(&to, p.out, p.out_low, D, ol) ? 1u : 0u;
+    p.tail_qb = 0;
+    if (p.causal && p.splits == 1 && p.q_blocks >= 4 && grid > 2 * slots) {
+        uint32_t t = (uint32_t)((2 * slots + BH - 1) / BH);
+        p.tail_qb = std::min<uint32_t>(t, p.q_blocks / 4);
+    }
     kernel<<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, to, p);
     count_launch(kernel_name("attn_fwd_kernel", {D, (int)a.mask_kind, QT}).c_str());
     if (p.splits > 1) {
