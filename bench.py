@@ -288,8 +288,20 @@ def _flush_l2(buf):
 
 def time_op(torch, fn, iters, flush_buf, stream, flush=True):
     """Average device time of fn over `iters` launches, L2 flushed before each
-    (flush=False: the call streams inputs larger than L2 itself)."""
+    (flush=False: the call streams inputs larger than L2 itself).  The device
+    first runs a sleep long enough for the host to enqueue every call, so each
+    event pair brackets device work only, not the host's cost of issuing the
+    next call (which exceeds the device time of short calls such as the
+    decode)."""
+    import time
+
+    t0 = time.perf_counter()
+    fn()  # enqueue cost of one call (nothing here synchronises)
+    host_s = time.perf_counter() - t0
+    torch.cuda.synchronize()
+    head_start_s = min(0.5, iters * (host_s + 1e-4) * 2 + 1e-3)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    torch.cuda._sleep(int(head_start_s * 2e9))  # cycles at up to ~2 GHz
     for a, b in evs:
         if flush:
             _flush_l2(flush_buf)
