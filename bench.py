@@ -288,20 +288,31 @@ def _flush_l2(buf):
 
 def time_op(torch, fn, iters, flush_buf, stream, flush=True):
     """Average device time of fn over `iters` launches, L2 flushed before each
-    (flush=False: the call streams inputs larger than L2 itself).  The device
-    first runs a sleep long enough for the host to enqueue every call, so each
-    event pair brackets device work only, not the host's cost of issuing the
-    next call (which exceeds the device time of short calls such as the
-    decode)."""
+    (flush=False: the call streams inputs larger than L2 itself).  Calls
+    whose host-side issue cost approaches their device time (the decode) are
+    preceded by 256 MB writes that need no host work, queued until the host
+    can enqueue every timed call ahead of the device, so each event pair
+    brackets device work only.  The lead is device work rather than an idle
+    sleep: an idle gap lets the next compute-bound kernels run above the
+    power-capped clocks they see in a busy stream."""
     import time
 
     t0 = time.perf_counter()
     fn()  # enqueue cost of one call (nothing here synchronises)
     host_s = time.perf_counter() - t0
     torch.cuda.synchronize()
-    head_start_s = min(0.5, iters * (host_s + 1e-4) * 2 + 1e-3)
+    # one call from an idle device: its issue cost plus its device time
+    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    fn()
+    b0.record(stream)
+    torch.cuda.synchronize()
+    span_s = a0.elapsed_time(b0) / 1e3
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-    torch.cuda._sleep(int(head_start_s * 2e9))  # cycles at up to ~2 GHz
+    if host_s > 0.3 * span_s:  # issue cost above ~40% of the device time
+        per_write_s = 60e-6  # one 256 MB read-modify-write, at most
+        for _ in range(min(400, int(iters * (host_s + 1e-4) * 2 / per_write_s) + 1)):
+            _flush_l2(flush_buf)
     for a, b in evs:
         if flush:
             _flush_l2(flush_buf)
