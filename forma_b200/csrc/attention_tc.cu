@@ -1787,7 +1787,7 @@ int launch_short(const AttnArgs& a, uint32_t fmt, const RowsLayout& ql, const Ro
     if (units > 0xffffffffull) return FB_ERR_UNSUPPORTED;
     const uint64_t grid = std::min<uint64_t>(units, (uint64_t)sm_count() * 2);  // persistent, two CTAs per SM
     kernel<<<(unsigned)grid, threads, smem, st>>>(tq, tk, tv, to, p);
-    count_launch("attn_short_kernel");
+    count_launch(split ? "attn_short_kernel<2>" : "attn_short_kernel");
     return launch_status("kernel launch");
 }
 }  // namespace

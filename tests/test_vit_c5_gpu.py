@@ -108,8 +108,8 @@ def test_c5_layer_kernels_are_the_tensor_core_ones(cuda):
     assert api.device_status() == 0
     kinds = {r for route in seen for r in route}
     assert "conv_gemm_pair_kernel<192,12>" in kinds  # QKV, fc1, proj, fc2
-    assert "attn_short_kernel" in kinds
+    assert "attn_short_kernel<2>" in kinds  # 197 keys: two softmax warps per query row
     assert "patches_vec8_kernel" in kinds and "rows_warp_kernel" in kinds
     simt = {"conv_direct_kernel", "attention_simt_kernel", "attention_part_kernel", "gemm_simt_kernel"}
     assert not (kinds & simt), kinds & simt
-    assert sum(1 for route in seen if "attn_short_kernel" in route) == cfg.layers
+    assert sum(1 for route in seen if "attn_short_kernel<2>" in route) == cfg.layers
