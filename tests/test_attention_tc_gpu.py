@@ -180,7 +180,8 @@ def test_tc_attention_additive_mask_per_head_causal(cuda):
 
 
 @pytest.mark.parametrize("case", ["ragged_129", "one_key", "full_256", "causal_masked_rows", "f16_negative_scale",
-                                  "gqa_packed_decode", "large_values"])
+                                  "gqa_packed_decode", "large_values", "split_f16_negative_scale",
+                                  "split_177_causal"])
 def test_short_key_range_kernel(cuda, case):
     """Key ranges of at most 256 at depth 64 (attn_short_kernel): key counts
     that are not multiples of the MMA step, a single key, a full 256-key row,
@@ -203,6 +204,13 @@ def test_short_key_range_kernel(cuda, case):
         check(cuda, (1, 3, 100, 64), (1, 3, 222, 64), (1, 3, 222, 64), scale=-0.09, dtype=torch.float16, **kw)
     elif case == "gqa_packed_decode":
         check(cuda, (2, 8, 3, 64), (2, 2, 200, 64), (2, 2, 200, 64), causal=150, expect=["attn_short_kernel<2>"])
+    elif case == "split_f16_negative_scale":
+        # two softmax warps per row with the row minimum as the logit maximum
+        check(cuda, (1, 3, 150, 64), (1, 3, 197, 64), (1, 3, 197, 64), scale=-0.09, dtype=torch.float16,
+              expect=["attn_short_kernel<2>"])
+    elif case == "split_177_causal":
+        # 177 keys: the second warp's last chunk holds one visible key of 16 columns
+        check(cuda, (2, 2, 200, 64), (2, 2, 177, 64), (2, 2, 177, 64), causal=-10, expect=["attn_short_kernel<2>"])
     else:
         out, ref = check(cuda, (1, 1, 128, 64), (1, 1, 250, 64), (1, 1, 250, 64), vconst=3.3e38, **kw)
         assert np.isfinite(out).all()
