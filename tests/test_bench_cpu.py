@@ -49,3 +49,27 @@ def test_reference_arm_under_torchrun_prints_on_rank_zero_only():
     lines = _json_lines(r.stdout)
     assert len(lines) == 1, r.stdout
     _check_line(lines[0], 2)
+
+
+def test_clock_summary_keeps_this_gpus_rows():
+    """The clocks key: median SM clock and the throttle reasons seen on this
+    process's GPU only (rows of other GPUs, by PCI bus id, are dropped)."""
+    import tempfile
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    rows = [
+        "0, 00000000:1B:00.0, 1965, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "1, 00000000:43:00.0, 1100, 1965, 300.0, 0x0, Active, Not Active, Not Active, Not Active",
+        "0, 00000000:1B:00.0, 1815, 1965, 998.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 00000000:1B:00.0, 1920, 1965, 990.5, 0x4, Not Active, Not Active, Not Active, Active",
+        "garbage line",
+    ]
+    s = bench.ClockSampler("00000000:1B:00.0", enabled=False)
+    s.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+    s.file.write("\n".join(rows) + "\n")
+    got = s.summary()
+    assert got == {"sm_mhz": 1920.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    # nothing sampled (no nvidia-smi): marked as such, never as clean clocks
+    assert bench.ClockSampler(None, enabled=False).summary()["reasons"] == ["unsampled"]
